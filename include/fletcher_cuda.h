@@ -1,0 +1,212 @@
+/*
+ * fletcher_cuda.h — C ABI of libcuda_fletcher.so, the B200 (sm_100a) backend for the
+ * embedding forward pass of longbow-fletcher.
+ *
+ * The library replaces the reference's CUDA shim (internal/device/cuda_bridge.h:17-53 +
+ * internal/device/cuda_backend.cu) behind the Go device.Backend / device.Tensor interface
+ * (internal/device/device.go:5-162).  The style of the reference bridge is kept: C linkage,
+ * opaque context and buffer handles, row-major (rows, cols) tensors, Linear weights stored
+ * (in, out), activation codes equal to device.ActivationType.  Differences:
+ *   - every call returns an int32 status (FLETCHER_OK = 0); Cuda_GetLastError gives the text,
+ *   - sizes are 64-bit,
+ *   - buffers carry a dtype (device.DataType plus BFloat16 = 2),
+ *   - variable-length attention, RoPE and pooling take per-sequence lengths,
+ *   - a whole-model entry point (Cuda_Model_*) runs BertModel.ForwardBatch
+ *     (internal/embeddings/model/bert.go:149-169) with fused kernels.
+ * Every call binds the context's device first, so calls may come from any host thread
+ * (goroutines migrate between OS threads).  Calls on one context are ordered on that
+ * context's stream; a context must not be used from two threads at the same time.
+ */
+#ifndef FLETCHER_CUDA_H
+#define FLETCHER_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with -fvisibility=hidden; everything declared here is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef void* CudaContextRef; /* cuda_bridge.h:14 */
+typedef void* CudaBufferRef;  /* cuda_bridge.h:15 */
+typedef void* CudaModelRef;
+
+/* ---- status codes */
+enum {
+  FLETCHER_OK = 0,
+  FLETCHER_ERR_INVALID = 1,     /* bad argument, shape or dtype */
+  FLETCHER_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  FLETCHER_ERR_OOM = 3,         /* device allocation failed */
+  FLETCHER_ERR_UNSUPPORTED = 4, /* shape/dtype combination this build does not handle */
+  FLETCHER_ERR_DEVICE_WAIT = 5  /* a kernel's bounded wait expired; the result is invalid */
+};
+
+/* ---- device.DataType (device.go:119-124) + BFloat16 */
+enum { FLETCHER_F32 = 0, FLETCHER_F16 = 1, FLETCHER_BF16 = 2 };
+
+/* ---- device.ActivationType (device.go:126-134) */
+enum {
+  FLETCHER_ACT_IDENTITY = 0,
+  FLETCHER_ACT_GELU = 1, /* GeluFast: tanh-GELU with the Pade tanh (simd.go:66-75) */
+  FLETCHER_ACT_TANH = 2, /* TanhFast (simd.go:49-63) */
+  FLETCHER_ACT_SOFTMAX = 3,
+  FLETCHER_ACT_SWIGLU = 4 /* silu(first half) * second half (cpu_backend.go:636-654) */
+};
+
+/* ---- pooling heads */
+enum {
+  FLETCHER_POOL_CLS_TANH = 0, /* BertPooler: CLS row -> Dense -> TanhFast (bert.go:441-488) */
+  FLETCHER_POOL_MEAN_L2 = 1   /* mean over each sequence's rows, then L2 normalisation */
+};
+
+/* BertConfig (bert.go:20-30) plus the RoPE base, which the reference hard-codes to 10000
+ * (cpu_backend.go:790).  position_type: 0 absolute (learned table), 1 RoPE. */
+typedef struct FletcherBertConfig {
+  int32_t vocab_size;
+  int32_t hidden;
+  int32_t num_layers;
+  int32_t num_heads;
+  int32_t intermediate;
+  int32_t max_positions;
+  int32_t activation;    /* FLETCHER_ACT_GELU or FLETCHER_ACT_SWIGLU */
+  int32_t position_type; /* 0 absolute, 1 RoPE */
+  float layer_norm_eps;
+  float rope_base;
+} FletcherBertConfig;
+
+/* ================================================================ context
+ * Cuda_Init: cuda_bridge.h:19.  Creates a context on device 0 with its own stream.
+ * Returns NULL when no CUDA device is usable. */
+CudaContextRef Cuda_Init(void);
+/* cuda_bridge.h:20; 0 when CUDA is unavailable. */
+int32_t Cuda_GetDeviceCount(void);
+/* cuda_bridge.h:21 (device.Backend.SetDevice, device.go:155).  Re-creates the stream on the
+ * new device; buffers made earlier stay on their device. */
+int32_t Cuda_SetDevice(CudaContextRef ctx, int32_t device);
+/* cuda_bridge.h:22 */
+void Cuda_FreeContext(CudaContextRef ctx);
+/* Copies the last error message of this context (NUL-terminated) into buf. */
+int32_t Cuda_GetLastError(CudaContextRef ctx, char* buf, int32_t len);
+/* cuda_bridge.h:51 (device.Backend.Synchronize, device.go:149).  Also reports a bounded
+ * device wait that expired since the last check (FLETCHER_ERR_DEVICE_WAIT). */
+int32_t Cuda_Synchronize(CudaContextRef ctx);
+/* The context's cudaStream_t, for callers that time or order work around it. */
+void* Cuda_GetStream(CudaContextRef ctx);
+/* device.Backend.GetVRAMUsage (device.go:161): bytes held by this context's buffers, and
+ * the device's total memory. */
+int32_t Cuda_MemGetInfo(CudaContextRef ctx, int64_t* allocated, int64_t* total);
+
+/* ================================================================ buffers
+ * Cuda_Alloc: cuda_bridge.h:25 (size in bytes, dtype f32).  Cuda_AllocTensor allocates
+ * rows*cols elements of dtype (device.Backend.NewTensorWithType, device.go:140).
+ * Memory comes from a stream-ordered pool and is zero-filled. */
+CudaBufferRef Cuda_Alloc(CudaContextRef ctx, int64_t size);
+CudaBufferRef Cuda_AllocTensor(CudaContextRef ctx, int64_t rows, int64_t cols, int32_t dtype);
+/* cuda_bridge.h:26 */
+int32_t Cuda_FreeBuffer(CudaContextRef ctx, CudaBufferRef buf);
+/* cuda_bridge.h:27-29: raw byte copies (synchronous with respect to the host). */
+int32_t Cuda_CopyToDevice(CudaBufferRef buf, int64_t offset, const void* data, int64_t size);
+int32_t Cuda_CopyToHost(CudaBufferRef buf, int64_t offset, void* data, int64_t size);
+/* cuda_bridge.h:30: the device pointer. */
+void* Cuda_GetBufferContents(CudaBufferRef buf);
+int32_t Cuda_BufferInfo(CudaBufferRef buf, int64_t* rows, int64_t* cols, int32_t* dtype);
+/* device.Tensor.CopyFromFloat32 / ToHost (device.go:24-27): float32 host data converted to
+ * or from the buffer's dtype on the device (cuda_linux.go:139-169 converts on the host). */
+int32_t Cuda_CopyFromFloat32(CudaBufferRef buf, const float* data, int64_t count);
+int32_t Cuda_ToHostFloat32(CudaBufferRef buf, float* data, int64_t count);
+
+/* ================================================================ tensor ops
+ * All tensors are row-major and dense.  Buffers of one op share a dtype except where noted
+ * (LayerNorm gamma/beta are always f32, as in bert.go:279-280). */
+
+/* cuda_bridge.h:33-36 (device.Tensor.Linear / LinearActivation, cpu_backend.go:612-660):
+ * result = act(input[rows,inCols] . weight[inCols,outCols] + bias).  For SwiGLU the
+ * result has outCols/2 columns.  bias may be NULL. */
+int32_t Cuda_Linear_Fused(CudaContextRef ctx, CudaBufferRef input, int64_t rows, int64_t inCols,
+                          CudaBufferRef weight, int64_t outCols, CudaBufferRef bias,
+                          CudaBufferRef result, int32_t activation);
+/* cuda_bridge.h:38-40 (cpu_backend.go:541-601).  input may equal result. */
+int32_t Cuda_LayerNorm(CudaContextRef ctx, CudaBufferRef input, CudaBufferRef gamma,
+                       CudaBufferRef beta, CudaBufferRef result, int64_t rows, int64_t cols,
+                       float eps);
+/* device.Tensor.AddLayerNorm (cpu_backend.go:603-610): x = LayerNorm(x + residual). */
+int32_t Cuda_AddLayerNorm(CudaContextRef ctx, CudaBufferRef x, CudaBufferRef residual,
+                          CudaBufferRef gamma, CudaBufferRef beta, int64_t rows, int64_t cols,
+                          float eps);
+/* cuda_bridge.h:42-43: SoftmaxFast per row (simd.go:78-99). */
+int32_t Cuda_Softmax(CudaContextRef ctx, CudaBufferRef input, CudaBufferRef result, int64_t rows,
+                     int64_t cols);
+/* cuda_bridge.h:45-46 (cpu_backend.go:496-510): output[i] = table[indices[i]].  indices is
+ * a host int32 array here (the Go caller holds []int). */
+int32_t Cuda_Gather(CudaContextRef ctx, CudaBufferRef table, const int32_t* indices,
+                    CudaBufferRef output, int64_t indicesCount, int64_t cols);
+/* Elementwise ops of device.Tensor (device.go:42-60), in place on x. */
+int32_t Cuda_Add(CudaContextRef ctx, CudaBufferRef x, CudaBufferRef other, int64_t count);
+int32_t Cuda_Scale(CudaContextRef ctx, CudaBufferRef x, float val, int64_t count);
+int32_t Cuda_AddScalar(CudaContextRef ctx, CudaBufferRef x, float val, int64_t count);
+int32_t Cuda_AddBias(CudaContextRef ctx, CudaBufferRef x, CudaBufferRef bias, int64_t rows,
+                     int64_t cols);
+int32_t Cuda_Activation(CudaContextRef ctx, CudaBufferRef x, int64_t rows, int64_t cols,
+                        int32_t activation);
+/* device.Tensor.Cast (device.go:111): dst = src converted to dst's dtype. */
+int32_t Cuda_Cast(CudaContextRef ctx, CudaBufferRef src, CudaBufferRef dst, int64_t count);
+/* device.Tensor.HasNaN (device.go:116): *result = 1 if any NaN or Inf. */
+int32_t Cuda_HasNaN(CudaContextRef ctx, CudaBufferRef x, int64_t count, int32_t* result);
+
+/* cuda_bridge.h:48-49 (device.Tensor.Attention, cpu_backend.go:662-758): uniform batches,
+ * q/k/v/result [batch*seqLen, hidden], numHeads heads, softmax(scale * Q K^T) V. */
+int32_t Cuda_Attention_Fused(CudaContextRef ctx, CudaBufferRef q, CudaBufferRef k,
+                             CudaBufferRef v, CudaBufferRef result, int64_t batchSize,
+                             int64_t seqLen, int64_t hidden, int32_t numHeads, float scale);
+/* device.Tensor.AttentionVarLen (device.go:92, cpu_backend.go:66-132): packed sequences
+ * of the given lengths (host array), per-sequence multi-head attention. */
+int32_t Cuda_Attention_VarLen(CudaContextRef ctx, CudaBufferRef q, CudaBufferRef k,
+                              CudaBufferRef v, CudaBufferRef result, const int32_t* lengths,
+                              int32_t numSeqs, int64_t hidden, int32_t numHeads, float scale);
+/* cuda_bridge.h:51-52 (cpu_backend.go:760-805): rotate-half RoPE in place, base 10000,
+ * position = row % seqLen. */
+int32_t Cuda_ApplyRoPE(CudaContextRef ctx, CudaBufferRef data, int64_t batchSize, int64_t seqLen,
+                       int32_t numHeads, int32_t headDim);
+/* RoPE over packed sequences: position = row index within its own sequence. */
+int32_t Cuda_ApplyRoPE_VarLen(CudaContextRef ctx, CudaBufferRef data, const int32_t* lengths,
+                              int32_t numSeqs, int32_t numHeads, int32_t headDim, float base);
+/* Mean pooling + L2 normalisation: hidden [sum(lengths), cols] -> out [numSeqs, cols] f32.
+ * (No counterpart in the reference; the spec's pooling head.) */
+int32_t Cuda_MeanPoolL2(CudaContextRef ctx, CudaBufferRef hidden, const int32_t* lengths,
+                        int32_t numSeqs, int64_t cols, CudaBufferRef out);
+
+/* ================================================================ whole model
+ * BertModel (bert.go:77-169) on the device, with fused kernels: tcgen05 GEMMs with fused
+ * epilogues (bias, RoPE, GELU/SwiGLU, residual) and flash attention for bf16/f16;
+ * fp32 SIMT kernels with the reference's fast-math formulas for f32. */
+int32_t Cuda_Model_Create(CudaContextRef ctx, const FletcherBertConfig* cfg, int32_t dtype,
+                          CudaModelRef* out);
+/* Loads weights from one host float32 blob in LoadFromRawBinary order
+ * (internal/embeddings/weights/loader.go:29-90); count must equal Cuda_Model_WeightCount. */
+int32_t Cuda_Model_LoadRaw(CudaModelRef model, const float* blob, int64_t count);
+int64_t Cuda_Model_WeightCount(const FletcherBertConfig* cfg);
+/* BertModel.ForwardBatch(ids, lengths) (bert.go:149): host ids (packed, sum(lengths)
+ * entries) and lengths in, host float32 out[numSeqs, hidden].  Synchronous. */
+int32_t Cuda_Model_ForwardBatch(CudaModelRef model, const int32_t* ids, const int32_t* lengths,
+                                int32_t numSeqs, int32_t pooling, float* out);
+/* Same pass with device-resident ids (int32, packed) and a device float32 output; lengths
+ * stay on the host (they shape the launch).  Asynchronous on the context's stream. */
+int32_t Cuda_Model_ForwardBatchDevice(CudaModelRef model, const int32_t* d_ids,
+                                      const int32_t* lengths, int32_t numSeqs, int32_t pooling,
+                                      float* d_out);
+/* Copies the last hidden state [sum(lengths), hidden] of the previous forward as float32. */
+int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count);
+int32_t Cuda_Model_Free(CudaModelRef model);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLETCHER_CUDA_H */

@@ -1,0 +1,127 @@
+// Shared definitions of libcuda_fletcher: context, buffers, error plumbing, dtype helpers.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <string>
+
+#include "../../include/fletcher_cuda.h"
+
+namespace fl {
+
+// Device-side error codes written to Ctx::d_err by kernels whose bounded waits expire.
+enum DeviceErr : int32_t { kDevOk = 0, kDevWaitTimeout = 1 };
+
+struct Ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int num_sms = 148;
+  int64_t allocated = 0;
+  int32_t* d_err = nullptr;  // device flag, set by kernels on a bounded-wait timeout
+  std::string last_error;
+};
+
+struct Buf {
+  Ctx* ctx = nullptr;
+  void* ptr = nullptr;
+  int64_t bytes = 0;
+  int64_t rows = 0, cols = 0;
+  int32_t dtype = FLETCHER_F32;
+};
+
+inline int64_t dtype_size(int32_t dt) { return dt == FLETCHER_F32 ? 4 : 2; }
+
+int32_t set_error(Ctx* c, int32_t code, const char* fmt, ...);
+
+// Binds the context's device for the duration of an ABI call.
+struct DeviceGuard {
+  explicit DeviceGuard(const Ctx* c) { cudaSetDevice(c->device); }
+};
+
+#define FL_CUDA(ctx, call)                                                                  \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess)                                                                  \
+      return ::fl::set_error((ctx), FLETCHER_ERR_CUDA, "%s failed: %s (%s:%d)", #call,      \
+                             cudaGetErrorString(e_), __FILE__, __LINE__);                   \
+  } while (0)
+
+#define FL_CHECK(ctx, cond, ...)                                                            \
+  do {                                                                                      \
+    if (!(cond)) return ::fl::set_error((ctx), FLETCHER_ERR_INVALID, __VA_ARGS__);          \
+  } while (0)
+
+#define FL_LAUNCH(ctx)                                                                      \
+  do {                                                                                      \
+    cudaError_t e_ = cudaGetLastError();                                                    \
+    if (e_ != cudaSuccess)                                                                  \
+      return ::fl::set_error((ctx), FLETCHER_ERR_CUDA, "kernel launch failed: %s (%s:%d)",  \
+                             cudaGetErrorString(e_), __FILE__, __LINE__);                   \
+  } while (0)
+
+// Allocation from the stream-ordered pool; zero-filled.
+int32_t dev_alloc(Ctx* c, void** p, int64_t bytes);
+void dev_free(Ctx* c, void* p, int64_t bytes);
+
+// ---------------------------------------------------------------- device helpers
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
+// The reference's fast-math helpers (internal/simd/simd.go), written with explicitly
+// rounded float operations so that the compiler cannot contract them into FMAs: the
+// results then match the Go code (which does not fuse on amd64) operation for operation.
+// ExpFast, simd.go:7-46.
+__device__ __forceinline__ float exp_fast(float x) {
+  if (x > 88.0f) return 1e38f;
+  if (x < -88.0f) return 0.0f;
+  float t = __fmul_rn(x, 1.442695f);
+  int k = (int)t;  // truncation toward zero, as Go's int(t)
+  if (t < 0.0f) k--;
+  float f = __fsub_rn(t, (float)k);
+  float p = __fadd_rn(1.0f, __fmul_rn(f, __fadd_rn(0.6931472f, __fmul_rn(f, __fadd_rn(0.2402265f, __fmul_rn(f, 0.0555041f))))));
+  // 2^k exactly; k is in [-128, 127] here, so 2^k may be subnormal.
+  float two_k = k >= -126 ? __int_as_float((k + 127) << 23) : __int_as_float(1 << (k + 149));
+  return __fmul_rn(p, two_k);
+}
+// TanhFast, simd.go:49-63.
+__device__ __forceinline__ float tanh_fast(float x) {
+  if (x > 4.0f) return 1.0f;
+  if (x < -4.0f) return -1.0f;
+  float x2 = __fmul_rn(x, x);
+  return __fdiv_rn(__fmul_rn(x, __fadd_rn(27.0f, x2)), __fadd_rn(27.0f, __fmul_rn(9.0f, x2)));
+}
+// GeluFast, simd.go:66-75: 0.5*x*(1 + TanhFast(0.7978846*(x + 0.044715*x^3))).
+__device__ __forceinline__ float gelu_fast(float x) {
+  float c3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+  float th = tanh_fast(__fmul_rn(0.7978846f, __fadd_rn(x, c3)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, th));
+}
+// SwiGLU element (cpu_backend.go:649-650): x / (1 + float32(exp(float64(-x)))) * y.
+__device__ __forceinline__ float swiglu_exact(float x, float y) {
+  float e = (float)exp(-(double)x);
+  return __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, e)), y);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace fl

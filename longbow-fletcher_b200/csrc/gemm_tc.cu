@@ -1,0 +1,490 @@
+// tcgen05 / TMEM / TMA GEMM for sm_100a: out = epilogue(A[M,K] . W[N,K]^T).
+//
+// The dense contractions of the encoder (QKV, attention output, FFN up and down; the
+// reference's Linear -> mulBLAS, cpu_backend.go:350-372, and Cuda_Linear_Fused,
+// cuda_backend.cu:65-92) run here in bf16 or fp16 with fp32 accumulation in tensor memory.
+//
+// Layout: A is the activation, row-major [M, K] (K contiguous).  W is the weight packed
+// K-major [N, K] at model load (the reference stores Linear weights (in, out) = [K, N]).
+// Both are fetched by TMA in 128-byte-swizzled 64-wide K slabs.
+//
+// Kernel structure (persistent, one CTA per SM, 192 threads):
+//   warp 0  : TMA producer — one thread streams A/W slabs into a STAGES-deep smem ring;
+//   warp 1  : MMA issuer — one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two
+//             TMEM accumulators and commits to mbarriers; the warp also owns TMEM alloc;
+//   warps 2-5: epilogue — tcgen05.ld the accumulator (each warp reads its 32-lane quarter),
+//             apply bias / RoPE / GELU / SwiGLU / residual in registers, store 16-bit rows.
+// Two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+// Every mbarrier wait is bounded: on expiry the kernel records an error in a device flag,
+// raises a CTA-wide abort flag and all roles leave their loops.
+// No TMA multicast is used.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "gemm.cuh"
+
+namespace fl {
+namespace tc {
+
+constexpr int BM = 128, BK = 64;
+constexpr long long kWaitLimitCycles = 4000000000LL;  // ~2 s at 2 GHz
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait.  Returns false when this CTA is aborting (timeout here or elsewhere).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int32_t* err) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 0) {
+      if (*abort) return false;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        atomicExch(err, kDevWaitTimeout);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05): K-major, 128-byte swizzle, 8-row groups 1024 B
+// apart (SBO), version 1, base offset 0.  The tile base must be 1024-byte aligned.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                   // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;         // SBO
+  d |= (uint64_t)1 << 46;                   // descriptor version
+  d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D f32, A/B bf16 (1) or f16 (0), both K-major.
+template <typename T, int BN>
+__device__ __forceinline__ uint32_t idesc() {
+  constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(id), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store32(T* dst, const float (&v)[32]) {
+  // 32 16-bit values = 64 bytes = 4 x 16-byte stores.
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; i++) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; i++) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
+template <typename T>
+__device__ __forceinline__ void load32(const T* src, float (&v)[32]) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    uint4 q = s[i];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
+        float2 f = __bfloat1622float2(h);
+        v[8 * i + 2 * j] = f.x;
+        v[8 * i + 2 * j + 1] = f.y;
+      } else {
+        __half2 h = *reinterpret_cast<const __half2*>(&w[j]);
+        float2 f = __half22float2(h);
+        v[8 * i + 2 * j] = f.x;
+        v[8 * i + 2 * j + 1] = f.y;
+      }
+    }
+  }
+}
+
+template <typename T, int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::STAGES;
+  uint64_t* tfull = bars + 2 * C::STAGES;
+  uint64_t* tempty = bars + 2 * C::STAGES + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 4);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = args.num_n_tiles;
+  const int num_tiles = args.num_m_tiles * n_tiles;
+  const int num_kb = args.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::STAGES; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int mb = tile / n_tiles, nb = tile % n_tiles;
+        for (int kb = 0; kb < num_kb; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort, args.err)) goto producer_done;
+          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, mb * BM);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id = idesc<T, BN>();
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort, args.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; kb++) {
+          if (!mbar_wait(&full[stage], phase, abort, args.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t a_desc = sw128_desc(smem_u32(sA + stage * C::A_BYTES));
+          const uint64_t b_desc = sw128_desc(smem_u32(sB + stage * C::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++)  // +32 bytes per K=16 step inside the swizzle atom
+            mma_f16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, id, (kb | k) != 0);
+          mma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // Epilogue warps 2..5; warp w may read TMEM lanes [32*(w%4), 32*(w%4)+32).
+    const int q = warp & 3;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int mb = tile / n_tiles, nb = tile % n_tiles;
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort, args.err)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)mb * BM + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      T* out = reinterpret_cast<T*>(args.out);
+      if constexpr (EPI == EPI_SWIGLU) {
+        // Tile columns [0, BN/2) hold gate rows, [BN/2, BN) the matching up rows.
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; c++) {
+          float g[32], u[32];
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + BN / 2 + c * 32, u);
+          const int pcol = nb * BN + c * 32;  // packed column of the gate chunk
+          const int64_t ocol = (int64_t)nb * (BN / 2) + c * 32;
+          if (row_ok && ocol < args.N / 2) {
+            if (args.bias) {
+#pragma unroll
+              for (int i = 0; i < 32; i++) {
+                g[i] += args.bias[pcol + i];
+                u[i] += args.bias[pcol + BN / 2 + i];
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i++) g[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * u[i];
+            store32<T>(out + row * args.ld_out + ocol, g);
+          }
+        }
+      } else if constexpr (EPI == EPI_ROPE) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; c++) {
+          float x1[32], x2[32];
+          tmem_ld32(tbase + c * 64, x1);
+          tmem_ld32(tbase + c * 64 + 32, x2);
+          const int64_t col = (int64_t)nb * BN + c * 64;
+          if (row_ok && col < args.N) {
+            if (args.bias) {
+#pragma unroll
+              for (int i = 0; i < 32; i++) {
+                x1[i] += args.bias[col + i];
+                x2[i] += args.bias[col + 32 + i];
+              }
+            }
+            if (col < args.rope_cols) {
+              const int p = args.pos[row];
+              const float* ct = args.cos_t + (int64_t)p * 32;
+              const float* st = args.sin_t + (int64_t)p * 32;
+#pragma unroll
+              for (int i = 0; i < 32; i++) {
+                const float a = x1[i], b = x2[i], cs = ct[i], sn = st[i];
+                x1[i] = a * cs - b * sn;
+                x2[i] = a * sn + b * cs;
+              }
+            }
+            store32<T>(out + row * args.ld_out + col, x1);
+            store32<T>(out + row * args.ld_out + col + 32, x2);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c++) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          const int64_t col = (int64_t)nb * BN + c * 32;
+          if (row_ok && col < args.N) {
+            if (args.bias) {
+#pragma unroll
+              for (int i = 0; i < 32; i++) v[i] += args.bias[col + i];
+            }
+            if constexpr (EPI == EPI_GELU) {
+#pragma unroll
+              for (int i = 0; i < 32; i++) v[i] = gelu_fast(v[i]);
+            }
+            if constexpr (EPI == EPI_RESIDUAL) {
+              float r[32];
+              load32<T>(reinterpret_cast<const T*>(args.residual) + row * args.ld_res + col, r);
+#pragma unroll
+              for (int i = 0; i < 32; i++) v[i] += r[i];
+            }
+            store32<T>(out + row * args.ld_out + col, v);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2D K-major map: dims {K, rows}, box {64, box_rows}, 128-byte swizzle, OOB reads as zero.
+static int32_t make_map(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, uint64_t rows, uint64_t K,
+                        uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(c, FLETCHER_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {K, rows};
+  cuuint64_t strides[1] = {K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dtype == FLETCHER_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(c, FLETCHER_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FLETCHER_OK;
+}
+
+template <typename T, int BN, int EPI>
+static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, GemmArgs a) {
+  using Cf = Cfg<BN>;
+  static bool attr_set[64] = {};  // per device
+  if (!attr_set[c->device & 63]) {
+    FL_CUDA(c, cudaFuncSetAttribute(k_gemm_tc<T, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
+    attr_set[c->device & 63] = true;
+  }
+  a.num_m_tiles = (int)((a.M + BM - 1) / BM);
+  a.num_n_tiles = (int)((a.N + BN - 1) / BN);
+  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  const int grid = tiles < c->num_sms ? tiles : c->num_sms;
+  k_gemm_tc<T, BN, EPI><<<grid, 192, Cf::SMEM, c->stream>>>(ma, mb, a);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+template <typename T>
+static int32_t dispatch(Ctx* c, int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a) {
+#define FL_EPI(E)                                                      \
+  case E:                                                              \
+    return bn == 256 ? run<T, 256, E>(c, ma, mb, a) : run<T, 128, E>(c, ma, mb, a);
+  switch (epi) {
+    FL_EPI(EPI_STORE)
+    FL_EPI(EPI_ROPE)
+    FL_EPI(EPI_GELU)
+    FL_EPI(EPI_SWIGLU)
+    FL_EPI(EPI_RESIDUAL)
+  }
+#undef FL_EPI
+  return set_error(c, FLETCHER_ERR_INVALID, "gemm: unknown epilogue %d", epi);
+}
+
+}  // namespace tc
+
+bool gemm_tc_supported(int64_t M, int64_t N, int64_t K, int bn) {
+  return M > 0 && K % tc::BK == 0 && K > 0 && N % 64 == 0 && (bn == 128 || bn == 256);
+}
+
+int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, int64_t M, int64_t K, const void* W,
+                       int64_t N, void* out, int64_t ld_out, const float* bias, const void* residual, int64_t ld_res,
+                       const int32_t* pos, const float* cos_t, const float* sin_t, int64_t rope_cols) {
+  FL_CHECK(c, dtype == FLETCHER_BF16 || dtype == FLETCHER_F16, "gemm_tc: 16-bit dtypes only");
+  FL_CHECK(c, gemm_tc_supported(M, N, K, bn), "gemm_tc: unsupported shape M=%lld N=%lld K=%lld BN=%d",
+           (long long)M, (long long)N, (long long)K, bn);
+  FL_CHECK(c, ((uintptr_t)A & 15) == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)out & 15) == 0 && ld_out % 8 == 0,
+           "gemm_tc: operands must be 16-byte aligned");
+  FL_CHECK(c, epi != EPI_SWIGLU || N % bn == 0, "gemm_tc: SwiGLU needs N %% BN == 0");
+  CUtensorMap ma, mb;
+  int32_t rc = tc::make_map(c, &ma, dtype, A, (uint64_t)M, (uint64_t)K, tc::BM);
+  if (rc) return rc;
+  rc = tc::make_map(c, &mb, dtype, W, (uint64_t)N, (uint64_t)K, (uint32_t)bn);
+  if (rc) return rc;
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = (int)K;
+  a.out = out;
+  a.ld_out = ld_out;
+  a.bias = bias;
+  a.residual = residual;
+  a.ld_res = ld_res;
+  a.pos = pos;
+  a.cos_t = cos_t;
+  a.sin_t = sin_t;
+  a.rope_cols = rope_cols;
+  a.err = c->d_err;
+  if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16>(c, epi, bn, ma, mb, a);
+  return tc::dispatch<__half>(c, epi, bn, ma, mb, a);
+}
+
+}  // namespace fl

@@ -1,0 +1,536 @@
+// Whole-model forward on the device: BertModel.ForwardBatch (bert.go:149-169) with fused
+// kernels, behind Cuda_Model_* of include/fletcher_cuda.h.
+//
+// Per layer (16-bit mode), 7 launches:
+//   QKV   = X . Wqkv^T (+b), RoPE on Q|K in the epilogue          (tcgen05 GEMM, EPI_ROPE)
+//   CTX   = flash-attention(QKV) over packed sequences            (mma.sync flash kernel)
+//   S     = CTX . Wo^T + bo + X                                   (tcgen05 GEMM, EPI_RESIDUAL)
+//   X     = LayerNorm(S)                                          (warp-per-row LN)
+//   ACT   = SwiGLU / GeluFast(X . Wi^T + bi)                      (tcgen05 GEMM, EPI_SWIGLU/GELU)
+//   S     = ACT . Wd^T + bd + X                                   (tcgen05 GEMM, EPI_RESIDUAL)
+//   X     = LayerNorm(S)
+// fp32 mode runs the same graph with the SIMT GEMM, a RoPE kernel and the fp32 attention
+// kernel, using the reference's fast-math formulas, for parity with its CPU path.
+// The residual stream X stays in the model dtype; LayerNorm statistics are fp32.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <vector>
+
+#include "gemm.cuh"
+
+namespace fl {
+
+struct Layer {
+  void* wqkv = nullptr;  // f32: (in,out) [H, 3H]; 16-bit: K-major [3H, H]
+  float* bqkv = nullptr;
+  void* wo = nullptr;
+  float* bo = nullptr;
+  float *ln1g = nullptr, *ln1b = nullptr;
+  void* wi = nullptr;  // f32: [H, Iup]; 16-bit: K-major [Iup, H] (SwiGLU gate/up interleaved)
+  float* bi = nullptr;
+  void* wd = nullptr;  // f32: [I, H]; 16-bit: K-major [H, I]
+  float* bd = nullptr;
+  float *ln2g = nullptr, *ln2b = nullptr;
+};
+
+struct Model {
+  Ctx* c = nullptr;
+  FletcherBertConfig cfg{};
+  int32_t dtype = FLETCHER_F32;
+  bool loaded = false;
+  int64_t H = 0, I = 0, Iup = 0, nh = 0, dh = 0;
+  int bn_qkv = 256, bn_o = 128, bn_up = 256, bn_d = 128;
+  std::vector<std::pair<void*, int64_t>> allocs;  // everything owned, freed at destroy
+  void* word = nullptr;
+  void* ptab = nullptr;
+  void* type0 = nullptr;
+  float *eln_g = nullptr, *eln_b = nullptr;
+  std::vector<Layer> layers;
+  float *wp = nullptr, *bp = nullptr;  // pooler in fp32 (bert.go:459-477 forces fp32)
+  float *cos_t = nullptr, *sin_t = nullptr;
+  int rope_len = 0;
+  // workspace
+  int64_t ws_T = 0;
+  int32_t ws_B = 0;
+  void *X = nullptr, *S = nullptr, *QKV = nullptr, *CTX = nullptr, *ACT = nullptr, *INTER = nullptr;
+  int32_t *d_ids = nullptr, *d_cu = nullptr, *d_pos = nullptr;
+  int2* d_tiles = nullptr;
+  int64_t tiles_cap = 0;
+  float* d_out = nullptr;
+  float* d_cls = nullptr;
+  std::vector<std::pair<void*, int64_t>> ws;
+  // pinned staging for per-batch metadata
+  uint8_t* h_meta = nullptr;
+  int64_t h_meta_cap = 0;
+  cudaEvent_t meta_done = nullptr;
+  int64_t last_T = 0;
+};
+
+static int32_t own(Model* m, void** p, int64_t bytes) {
+  int32_t rc = dev_alloc(m->c, p, bytes);
+  if (rc == FLETCHER_OK) m->allocs.push_back({*p, bytes});
+  return rc;
+}
+
+static void free_ws(Model* m) {
+  for (auto& a : m->ws) dev_free(m->c, a.first, a.second);
+  m->ws.clear();
+  m->ws_T = 0;
+  m->ws_B = 0;
+}
+
+static int32_t ws_alloc(Model* m, void** p, int64_t bytes) {
+  int32_t rc = dev_alloc(m->c, p, bytes);
+  if (rc == FLETCHER_OK) m->ws.push_back({*p, bytes});
+  return rc;
+}
+
+static int32_t ensure_ws(Model* m, int64_t T, int32_t B) {
+  if (T <= m->ws_T && B <= m->ws_B) return FLETCHER_OK;
+  free_ws(m);
+  const int64_t Tc = std::max<int64_t>(T, 128), Bc = std::max<int32_t>(B, 64);
+  const int64_t es = dtype_size(m->dtype);
+  int32_t rc = 0;
+  if ((rc = ws_alloc(m, &m->X, Tc * m->H * es))) return rc;
+  if ((rc = ws_alloc(m, &m->S, Tc * m->H * es))) return rc;
+  if ((rc = ws_alloc(m, &m->QKV, Tc * 3 * m->H * es))) return rc;
+  if ((rc = ws_alloc(m, &m->CTX, Tc * m->H * es))) return rc;
+  if ((rc = ws_alloc(m, &m->ACT, Tc * m->I * es))) return rc;
+  if (m->dtype == FLETCHER_F32 && (rc = ws_alloc(m, &m->INTER, Tc * m->Iup * es))) return rc;
+  if ((rc = ws_alloc(m, (void**)&m->d_ids, Tc * 4))) return rc;
+  if ((rc = ws_alloc(m, (void**)&m->d_pos, Tc * 4))) return rc;
+  if ((rc = ws_alloc(m, (void**)&m->d_cu, (Bc + 1) * 4))) return rc;
+  m->tiles_cap = Tc / 64 + Bc + 1;
+  if ((rc = ws_alloc(m, (void**)&m->d_tiles, m->tiles_cap * 8))) return rc;
+  if ((rc = ws_alloc(m, (void**)&m->d_out, Bc * m->H * 4))) return rc;
+  if ((rc = ws_alloc(m, (void**)&m->d_cls, Bc * m->H * 4))) return rc;
+  m->ws_T = Tc;
+  m->ws_B = (int32_t)Bc;
+  return FLETCHER_OK;
+}
+
+static int32_t ensure_rope(Model* m, int32_t need) {
+  if (m->cfg.position_type != 1 || need <= m->rope_len) return FLETCHER_OK;
+  int32_t len = std::max<int32_t>(need, m->cfg.max_positions);
+  if (m->cos_t) {
+    dev_free(m->c, m->cos_t, (int64_t)m->rope_len * (m->dh / 2) * 4);
+    dev_free(m->c, m->sin_t, (int64_t)m->rope_len * (m->dh / 2) * 4);
+    m->cos_t = m->sin_t = nullptr;
+  }
+  int32_t rc;
+  if ((rc = dev_alloc(m->c, (void**)&m->cos_t, (int64_t)len * (m->dh / 2) * 4))) return rc;
+  if ((rc = dev_alloc(m->c, (void**)&m->sin_t, (int64_t)len * (m->dh / 2) * 4))) return rc;
+  m->rope_len = len;
+  return launch_rope_build_table(m->c, m->cos_t, m->sin_t, len, (int32_t)m->dh, (double)m->cfg.rope_base);
+}
+
+int64_t weight_count(const FletcherBertConfig* c) {
+  const int64_t H = c->hidden, I = c->intermediate, Iup = c->activation == FLETCHER_ACT_SWIGLU ? 2 * I : I;
+  int64_t n = (int64_t)c->vocab_size * H + (int64_t)c->max_positions * H + 2 * H + 2 * H;
+  const int64_t per = 3 * (H * H + H) + (H * H + H) + 2 * H + (H * Iup + Iup) + (I * H + H) + 2 * H;
+  return n + per * c->num_layers + H * H + H;
+}
+
+// Uploads n fp32 host values to a fresh device array.
+static int32_t up_f32(Model* m, float** d, const float* h, int64_t n) {
+  int32_t rc = own(m, (void**)d, n * 4);
+  if (rc) return rc;
+  FL_CUDA(m->c, cudaMemcpyAsync(*d, h, n * 4, cudaMemcpyHostToDevice, m->c->stream));
+  return FLETCHER_OK;
+}
+
+static bool all_zero(const float* p, int64_t n) {
+  for (int64_t i = 0; i < n; i++)
+    if (p[i] != 0.0f) return false;
+  return true;
+}
+
+// A Linear weight (in,out) = [K, N] fp32 on the host -> the layout the GEMM of this dtype
+// reads: fp32 (in,out) as is; 16-bit K-major [N, K] (optionally SwiGLU-interleaved).
+static int32_t up_weight(Model* m, void** d, const float* h, int64_t K, int64_t N, int perm, int bn, float* staging) {
+  Ctx* c = m->c;
+  if (m->dtype == FLETCHER_F32) return up_f32(m, (float**)d, h, K * N);
+  int32_t rc = own(m, d, K * N * 2);
+  if (rc) return rc;
+  FL_CUDA(c, cudaMemcpyAsync(staging, h, K * N * 4, cudaMemcpyHostToDevice, c->stream));
+  rc = launch_pack_weight_kmajor(c, staging, K, N, *d, m->dtype, perm, bn);
+  if (rc) return rc;
+  FL_CUDA(c, cudaStreamSynchronize(c->stream));  // staging is reused by the next weight
+  return FLETCHER_OK;
+}
+
+static int32_t up_table(Model* m, void** d, const float* h, int64_t n, float* staging) {
+  Ctx* c = m->c;
+  if (m->dtype == FLETCHER_F32) return up_f32(m, (float**)d, h, n);
+  int32_t rc = own(m, d, n * 2);
+  if (rc) return rc;
+  const int64_t chunk = 64ll << 20;  // staging holds at most `chunk` floats
+  for (int64_t o = 0; o < n; o += chunk) {
+    const int64_t k = std::min(chunk, n - o);
+    FL_CUDA(c, cudaMemcpyAsync(staging, h + o, k * 4, cudaMemcpyHostToDevice, c->stream));
+    rc = convert_from_f32(c, staging, (uint8_t*)*d + o * 2, m->dtype, k);
+    if (rc) return rc;
+    FL_CUDA(c, cudaStreamSynchronize(c->stream));
+  }
+  return FLETCHER_OK;
+}
+
+static int32_t load_raw(Model* m, const float* blob, int64_t count) {
+  Ctx* c = m->c;
+  const FletcherBertConfig& cf = m->cfg;
+  FL_CHECK(c, count == weight_count(&cf), "LoadRaw: %lld values, expected %lld", (long long)count,
+           (long long)weight_count(&cf));
+  const int64_t H = m->H, I = m->I, Iup = m->Iup;
+  const float* p = blob;
+  auto take = [&](int64_t n) {
+    const float* r = p;
+    p += n;
+    return r;
+  };
+  float* staging = nullptr;
+  const int64_t stage_n = std::max<int64_t>({H * 3 * H, H * Iup, I * H, 64ll << 20});
+  int32_t rc = dev_alloc(c, (void**)&staging, stage_n * 4);
+  if (rc) return rc;
+  struct StageFree {
+    Ctx* c;
+    float* p;
+    int64_t n;
+    ~StageFree() { dev_free(c, p, n * 4); }
+  } sf{c, staging, stage_n};
+
+  const float* word = take((int64_t)cf.vocab_size * H);
+  const float* pos = take((int64_t)cf.max_positions * H);
+  const float* type = take(2 * H);
+  const float* eg = take(H);
+  const float* eb = take(H);
+  if ((rc = up_table(m, &m->word, word, (int64_t)cf.vocab_size * H, staging))) return rc;
+  if (cf.position_type == 0 && (rc = up_table(m, &m->ptab, pos, (int64_t)cf.max_positions * H, staging))) return rc;
+  if ((rc = up_table(m, &m->type0, type, H, staging))) return rc;  // token type 0 only (bert.go:242-245)
+  if ((rc = up_f32(m, &m->eln_g, eg, H))) return rc;
+  if ((rc = up_f32(m, &m->eln_b, eb, H))) return rc;
+
+  std::vector<float> cat((size_t)(H * 3 * H));
+  std::vector<float> bcat((size_t)(3 * H));
+  std::vector<float> bip((size_t)Iup);
+  m->layers.assign(cf.num_layers, Layer());
+  for (int l = 0; l < cf.num_layers; l++) {
+    Layer& L = m->layers[l];
+    const float* wq = take(H * H); const float* bq = take(H);
+    const float* wk = take(H * H); const float* bk = take(H);
+    const float* wv = take(H * H); const float* bv = take(H);
+    const float* wo = take(H * H); const float* bo = take(H);
+    const float* l1g = take(H);    const float* l1b = take(H);
+    const float* wi = take(H * Iup); const float* bi = take(Iup);
+    const float* wd = take(I * H);   const float* bd = take(H);
+    const float* l2g = take(H);    const float* l2b = take(H);
+    // [Wq | Wk | Wv] as one (in,out) [H, 3H] matrix: the three Linear calls of bert.go:614-616
+    // become one GEMM with identical per-column dot products.
+    for (int64_t k = 0; k < H; k++) {
+      memcpy(&cat[k * 3 * H], wq + k * H, H * 4);
+      memcpy(&cat[k * 3 * H + H], wk + k * H, H * 4);
+      memcpy(&cat[k * 3 * H + 2 * H], wv + k * H, H * 4);
+    }
+    memcpy(&bcat[0], bq, H * 4);
+    memcpy(&bcat[H], bk, H * 4);
+    memcpy(&bcat[2 * H], bv, H * 4);
+    if ((rc = up_weight(m, &L.wqkv, cat.data(), H, 3 * H, 0, 0, staging))) return rc;
+    if (!all_zero(bcat.data(), 3 * H) && (rc = up_f32(m, &L.bqkv, bcat.data(), 3 * H))) return rc;
+    if ((rc = up_weight(m, &L.wo, wo, H, H, 0, 0, staging))) return rc;
+    if (!all_zero(bo, H) && (rc = up_f32(m, &L.bo, bo, H))) return rc;
+    if ((rc = up_f32(m, &L.ln1g, l1g, H))) return rc;
+    if ((rc = up_f32(m, &L.ln1b, l1b, H))) return rc;
+    const bool swiglu = cf.activation == FLETCHER_ACT_SWIGLU;
+    const bool interleave = swiglu && m->dtype != FLETCHER_F32;
+    if ((rc = up_weight(m, &L.wi, wi, H, Iup, interleave ? 1 : 0, m->bn_up, staging))) return rc;
+    if (!all_zero(bi, Iup)) {
+      if (interleave) {  // same interleave as the weight rows
+        const int64_t half = m->bn_up / 2;
+        for (int64_t n = 0; n < Iup; n++) {
+          const int64_t j = n / m->bn_up, r = n % m->bn_up;
+          bip[n] = bi[r < half ? j * half + r : I + j * half + (r - half)];
+        }
+        if ((rc = up_f32(m, &L.bi, bip.data(), Iup))) return rc;
+      } else if ((rc = up_f32(m, &L.bi, bi, Iup))) {
+        return rc;
+      }
+    }
+    if ((rc = up_weight(m, &L.wd, wd, I, H, 0, 0, staging))) return rc;
+    if (!all_zero(bd, H) && (rc = up_f32(m, &L.bd, bd, H))) return rc;
+    if ((rc = up_f32(m, &L.ln2g, l2g, H))) return rc;
+    if ((rc = up_f32(m, &L.ln2b, l2b, H))) return rc;
+  }
+  const float* wp = take(H * H);
+  const float* bp = take(H);
+  if ((rc = up_f32(m, &m->wp, wp, H * H))) return rc;
+  if ((rc = up_f32(m, &m->bp, bp, H))) return rc;
+  if ((rc = ensure_rope(m, cf.max_positions))) return rc;
+  FL_CUDA(c, cudaStreamSynchronize(c->stream));
+  m->loaded = true;
+  return FLETCHER_OK;
+}
+
+// Per-batch metadata -> device: cu_seqlens [B+1] and the attention tile list, through one
+// pinned staging buffer and one copy.
+static int32_t upload_meta(Model* m, const int32_t* lengths, int32_t B, int64_t T, int32_t* n_tiles, int32_t* max_len) {
+  Ctx* c = m->c;
+  std::vector<int32_t> order(B);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return lengths[a] > lengths[b]; });
+  int64_t nt = 0;
+  int32_t mx = 0;
+  for (int i = 0; i < B; i++) {
+    nt += (lengths[i] + 63) / 64;
+    mx = std::max(mx, lengths[i]);
+  }
+  FL_CHECK(c, nt <= m->tiles_cap, "internal: tile list overflow");
+  const int64_t bytes = (int64_t)(B + 1) * 4 + nt * 8 + 16;
+  if (bytes > m->h_meta_cap) {
+    if (m->h_meta) {
+      cudaEventSynchronize(m->meta_done);
+      cudaFreeHost(m->h_meta);
+    }
+    const int64_t cap = std::max<int64_t>(bytes * 2, 1 << 16);
+    FL_CUDA(c, cudaMallocHost((void**)&m->h_meta, cap));
+    m->h_meta_cap = cap;
+  } else {
+    FL_CUDA(c, cudaEventSynchronize(m->meta_done));  // previous batch's copy has consumed it
+  }
+  int32_t* cu = reinterpret_cast<int32_t*>(m->h_meta);
+  cu[0] = 0;
+  for (int i = 0; i < B; i++) cu[i + 1] = cu[i] + lengths[i];
+  const int64_t tiles_off = ((int64_t)(B + 1) * 4 + 15) / 16 * 16;
+  int2* tl = reinterpret_cast<int2*>(m->h_meta + tiles_off);
+  int64_t k = 0;
+  for (int oi = 0; oi < B; oi++) {
+    const int s = order[oi];
+    for (int q0 = 0; q0 < lengths[s]; q0 += 64) tl[k++] = make_int2(s, q0);
+  }
+  FL_CUDA(c, cudaMemcpyAsync(m->d_cu, cu, (B + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+  if (nt) FL_CUDA(c, cudaMemcpyAsync(m->d_tiles, tl, nt * 8, cudaMemcpyHostToDevice, c->stream));
+  FL_CUDA(c, cudaEventRecord(m->meta_done, c->stream));
+  *n_tiles = (int32_t)nt;
+  *max_len = mx;
+  (void)T;
+  return FLETCHER_OK;
+}
+
+static int32_t forward_device(Model* m, const int32_t* d_ids, const int32_t* lengths, int32_t B, int32_t pooling,
+                              float* d_out) {
+  Ctx* c = m->c;
+  FL_CHECK(c, m->loaded, "model weights are not loaded");
+  FL_CHECK(c, B > 0 && lengths != nullptr, "ForwardBatch: empty batch");
+  FL_CHECK(c, pooling == FLETCHER_POOL_CLS_TANH || pooling == FLETCHER_POOL_MEAN_L2, "unknown pooling %d", pooling);
+  int64_t T = 0;
+  for (int i = 0; i < B; i++) {
+    FL_CHECK(c, lengths[i] >= 0, "negative length");
+    T += lengths[i];
+  }
+  FL_CHECK(c, T > 0, "ForwardBatch: no tokens");
+  if (pooling == FLETCHER_POOL_CLS_TANH) FL_CHECK(c, lengths[B - 1] > 0, "CLS pooling of an empty last sequence");
+  int32_t rc = ensure_ws(m, T, B);
+  if (rc) return rc;
+  int32_t n_tiles = 0, max_len = 0;
+  if ((rc = upload_meta(m, lengths, B, T, &n_tiles, &max_len))) return rc;
+  if ((rc = ensure_rope(m, max_len))) return rc;
+  if ((rc = launch_positions(c, m->d_cu, B, m->d_pos, max_len))) return rc;
+  m->last_T = T;
+
+  const int64_t H = m->H, I = m->I, Iup = m->Iup;
+  const int32_t dt = m->dtype;
+  const float eps = m->cfg.layer_norm_eps;
+  const bool rope = m->cfg.position_type == 1;
+  if ((rc = launch_embed(c, dt, d_ids, m->d_pos, m->word, rope ? nullptr : m->ptab, m->cfg.max_positions, m->type0,
+                         m->eln_g, m->eln_b, m->X, T, H, eps)))
+    return rc;
+  const int64_t es = dtype_size(dt);
+  const float scale = 1.0f / (float)std::sqrt((double)m->dh);
+  const bool swiglu = m->cfg.activation == FLETCHER_ACT_SWIGLU;
+  for (auto& L : m->layers) {
+    if (dt == FLETCHER_F32) {
+      if ((rc = launch_sgemm(c, (float*)m->X, H, (float*)L.wqkv, 3 * H, (float*)m->QKV, 3 * H, T, 3 * H, H, L.bqkv,
+                             FLETCHER_ACT_IDENTITY)))
+        return rc;
+      if (rope && (rc = launch_rope_table(c, dt, m->QKV, T, 3 * H, 2 * H, (int32_t)m->dh, m->d_pos, m->cos_t, m->sin_t)))
+        return rc;
+      float* qkv = (float*)m->QKV;
+      if ((rc = launch_attention_f32(c, qkv, qkv + H, qkv + 2 * H, 3 * H, (float*)m->CTX, H, m->d_cu, B, T,
+                                     (int32_t)m->nh, (int32_t)m->dh, scale, max_len)))
+        return rc;
+      if ((rc = launch_sgemm(c, (float*)m->CTX, H, (float*)L.wo, H, (float*)m->S, H, T, H, H, L.bo, FLETCHER_ACT_IDENTITY)))
+        return rc;
+      if ((rc = launch_add_layernorm(c, dt, m->X, m->S, m->X, L.ln1g, L.ln1b, T, H, eps))) return rc;
+      if ((rc = launch_sgemm(c, (float*)m->X, H, (float*)L.wi, Iup, (float*)m->INTER, Iup, T, Iup, H, L.bi,
+                             swiglu ? FLETCHER_ACT_IDENTITY : FLETCHER_ACT_GELU)))
+        return rc;
+      const float* a_in = (float*)m->INTER;
+      if (swiglu) {
+        if ((rc = launch_swiglu(c, dt, m->INTER, m->ACT, T, I))) return rc;
+        a_in = (float*)m->ACT;
+      }
+      if ((rc = launch_sgemm(c, a_in, I, (float*)L.wd, H, (float*)m->S, H, T, H, I, L.bd, FLETCHER_ACT_IDENTITY)))
+        return rc;
+      if ((rc = launch_add_layernorm(c, dt, m->X, m->S, m->X, L.ln2g, L.ln2b, T, H, eps))) return rc;
+    } else {
+      const bool fuse_rope = rope && m->dh == 64;
+      if ((rc = launch_gemm_tc(c, dt, fuse_rope ? EPI_ROPE : EPI_STORE, m->bn_qkv, m->X, T, H, L.wqkv, 3 * H, m->QKV,
+                               3 * H, L.bqkv, nullptr, 0, m->d_pos, m->cos_t, m->sin_t, rope ? 2 * H : 0)))
+        return rc;
+      if (rope && !fuse_rope &&
+          (rc = launch_rope_table(c, dt, m->QKV, T, 3 * H, 2 * H, (int32_t)m->dh, m->d_pos, m->cos_t, m->sin_t)))
+        return rc;
+      const uint8_t* qkv = (const uint8_t*)m->QKV;
+      if ((rc = launch_flash_attention_ld(c, dt, qkv, qkv + H * es, qkv + 2 * H * es, 3 * H, m->CTX, H, m->d_cu,
+                                          m->d_tiles, n_tiles, (int32_t)m->nh, scale)))
+        return rc;
+      if ((rc = launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_o, m->CTX, T, H, L.wo, H, m->S, H, L.bo, m->X, H, nullptr,
+                               nullptr, nullptr, 0)))
+        return rc;
+      if ((rc = launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln1g, L.ln1b, T, H, eps))) return rc;
+      if ((rc = launch_gemm_tc(c, dt, swiglu ? EPI_SWIGLU : EPI_GELU, m->bn_up, m->X, T, H, L.wi, Iup, m->ACT, I, L.bi,
+                               nullptr, 0, nullptr, nullptr, nullptr, 0)))
+        return rc;
+      if ((rc = launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_d, m->ACT, T, I, L.wd, H, m->S, H, L.bd, m->X, H, nullptr,
+                               nullptr, nullptr, 0)))
+        return rc;
+      if ((rc = launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln2g, L.ln2b, T, H, eps))) return rc;
+    }
+  }
+  if (pooling == FLETCHER_POOL_MEAN_L2) return launch_mean_pool_l2(c, dt, m->X, m->d_cu, B, H, d_out);
+  // BertPooler.ForwardBatch (bert.go:441-488): CLS rows at cu_seqlens[i] -> fp32 Dense -> TanhFast.
+  if ((rc = launch_gather_rows_f32(c, dt, m->X, m->d_cu, B, H, m->d_cls))) return rc;
+  return launch_sgemm(c, m->d_cls, H, m->wp, H, d_out, H, B, H, H, m->bp, FLETCHER_ACT_TANH);
+}
+
+static int32_t create(Ctx* c, const FletcherBertConfig* cfg, int32_t dtype, Model** out) {
+  FL_CHECK(c, cfg && out, "Model_Create: null argument");
+  FL_CHECK(c, dtype >= 0 && dtype <= 2, "Model_Create: bad dtype %d", dtype);
+  FL_CHECK(c, cfg->hidden > 0 && cfg->num_heads > 0 && cfg->hidden % cfg->num_heads == 0, "bad hidden/heads");
+  FL_CHECK(c, cfg->activation == FLETCHER_ACT_GELU || cfg->activation == FLETCHER_ACT_SWIGLU,
+           "activation must be GELU or SwiGLU");
+  FL_CHECK(c, cfg->vocab_size > 0 && cfg->max_positions > 0 && cfg->num_layers >= 0, "bad config");
+  const int64_t dh = cfg->hidden / cfg->num_heads;
+  if (dtype != FLETCHER_F32) {
+    if (dh != 64 || cfg->hidden % 64 != 0 || cfg->intermediate % 128 != 0)
+      return set_error(c, FLETCHER_ERR_UNSUPPORTED,
+                       "16-bit model path needs head_dim 64, hidden %% 64 == 0, intermediate %% 128 == 0");
+  }
+  Model* m = new Model();
+  m->c = c;
+  m->cfg = *cfg;
+  m->dtype = dtype;
+  m->H = cfg->hidden;
+  m->I = cfg->intermediate;
+  m->Iup = cfg->activation == FLETCHER_ACT_SWIGLU ? 2 * m->I : m->I;
+  m->nh = cfg->num_heads;
+  m->dh = dh;
+  // Tile widths: 256-wide tiles for the wide GEMMs, 128 where N is small.
+  m->bn_qkv = (3 * m->H) % 256 == 0 && 3 * m->H >= 1024 ? 256 : 128;
+  m->bn_o = 128;
+  m->bn_d = 128;
+  m->bn_up = m->Iup % 256 == 0 && m->Iup >= 1024 ? 256 : 128;
+  if (cudaEventCreateWithFlags(&m->meta_done, cudaEventDisableTiming) != cudaSuccess) {
+    delete m;
+    return set_error(c, FLETCHER_ERR_CUDA, "cudaEventCreate failed");
+  }
+  cudaEventRecord(m->meta_done, c->stream);
+  *out = m;
+  return FLETCHER_OK;
+}
+
+static void destroy(Model* m) {
+  Ctx* c = m->c;
+  cudaStreamSynchronize(c->stream);
+  free_ws(m);
+  for (auto& a : m->allocs) dev_free(c, a.first, a.second);
+  if (m->cos_t) dev_free(c, m->cos_t, (int64_t)m->rope_len * (m->dh / 2) * 4);
+  if (m->sin_t) dev_free(c, m->sin_t, (int64_t)m->rope_len * (m->dh / 2) * 4);
+  cudaStreamSynchronize(c->stream);
+  if (m->h_meta) cudaFreeHost(m->h_meta);
+  if (m->meta_done) cudaEventDestroy(m->meta_done);
+  delete m;
+}
+
+}  // namespace fl
+
+using namespace fl;
+
+extern "C" {
+
+int64_t Cuda_Model_WeightCount(const FletcherBertConfig* cfg) { return cfg ? weight_count(cfg) : -1; }
+
+int32_t Cuda_Model_Create(CudaContextRef ctx, const FletcherBertConfig* cfg, int32_t dtype, CudaModelRef* out) {
+  Ctx* c = reinterpret_cast<Ctx*>(ctx);
+  if (!c) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(c);
+  Model* m = nullptr;
+  int32_t rc = create(c, cfg, dtype, &m);
+  if (rc == FLETCHER_OK) *out = m;
+  return rc;
+}
+
+int32_t Cuda_Model_LoadRaw(CudaModelRef model, const float* blob, int64_t count) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m || !blob) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(m->c);
+  return load_raw(m, blob, count);
+}
+
+int32_t Cuda_Model_ForwardBatchDevice(CudaModelRef model, const int32_t* d_ids, const int32_t* lengths, int32_t B,
+                                      int32_t pooling, float* d_out) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(m->c);
+  return forward_device(m, d_ids, lengths, B, pooling, d_out);
+}
+
+int32_t Cuda_Model_ForwardBatch(CudaModelRef model, const int32_t* ids, const int32_t* lengths, int32_t B,
+                                int32_t pooling, float* out) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m || !ids || !lengths || !out) return FLETCHER_ERR_INVALID;
+  Ctx* c = m->c;
+  DeviceGuard g(c);
+  FL_CHECK(c, B > 0, "ForwardBatch: empty batch");
+  int64_t T = 0;
+  for (int i = 0; i < B; i++) T += lengths[i] > 0 ? lengths[i] : 0;
+  for (int64_t t = 0; t < T; t++)
+    FL_CHECK(c, ids[t] >= 0 && ids[t] < m->cfg.vocab_size, "Gather index out of bounds: ids[%lld]=%d",
+             (long long)t, ids[t]);
+  int32_t rc = ensure_ws(m, T, B);
+  if (rc) return rc;
+  FL_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, T * 4, cudaMemcpyHostToDevice, c->stream));
+  if ((rc = forward_device(m, m->d_ids, lengths, B, pooling, m->d_out))) return rc;
+  FL_CUDA(c, cudaMemcpyAsync(out, m->d_out, (int64_t)B * m->H * 4, cudaMemcpyDeviceToHost, c->stream));
+  FL_CUDA(c, cudaStreamSynchronize(c->stream));
+  return check_device_flag(c);
+}
+
+int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m || !host_out) return FLETCHER_ERR_INVALID;
+  Ctx* c = m->c;
+  DeviceGuard g(c);
+  FL_CHECK(c, count <= m->last_T * m->H, "LastHidden: count exceeds the last batch");
+  float* tmp = nullptr;
+  int32_t rc = dev_alloc(c, (void**)&tmp, count * 4);
+  if (rc) return rc;
+  rc = convert_to_f32(c, m->X, m->dtype, tmp, count);
+  if (rc == FLETCHER_OK) {
+    cudaMemcpyAsync(host_out, tmp, count * 4, cudaMemcpyDeviceToHost, c->stream);
+    cudaStreamSynchronize(c->stream);
+  }
+  dev_free(c, tmp, count * 4);
+  FL_CUDA(c, cudaStreamSynchronize(c->stream));
+  return rc;
+}
+
+int32_t Cuda_Model_Free(CudaModelRef model) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m) return FLETCHER_OK;
+  DeviceGuard g(m->c);
+  destroy(m);
+  return FLETCHER_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,577 @@
+// Memory-bound kernels: embedding + LayerNorm, residual + LayerNorm, RoPE, SwiGLU, pooling,
+// softmax, elementwise, casts and weight packing.  One warp owns one row where rows are short
+// (LayerNorm, embedding), with 128-bit vector loads and warp-shuffle reductions; fp32
+// statistics throughout.
+#include <algorithm>
+
+#include "kernels.cuh"
+
+namespace fl {
+
+template <typename T, int VEC>
+struct alignas(sizeof(T) * VEC) Vec {
+  T d[VEC];
+};
+
+static inline int grid_for(int64_t n, int threads, int cap = 8192) {
+  int64_t b = (n + threads - 1) / threads;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(b, cap));
+}
+
+// ---------------------------------------------------------------- LayerNorm core
+// Two-pass statistics over the row held in registers (cpu_backend.go:579-600):
+// mean = sum/c, var = sum((x-mean)^2)/c, invStd = 1/float32(sqrt(float64(var+eps))),
+// y = (x-mean)*invStd*gamma + beta.  Sums are warp-tree reductions (order differs from the
+// reference's sequential sum by rounding only).
+template <typename T, int PER, int VEC>
+__device__ __forceinline__ void ln_finish(float (&v)[PER], int lane, int cols, const float* __restrict__ g,
+                                          const float* __restrict__ b, float eps, T* __restrict__ orow) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; i++) s += v[i];
+  s = warp_sum(s);
+  const float mean = __fdiv_rn(s, (float)cols);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    float d = __fsub_rn(v[i], mean);
+    q = __fadd_rn(q, __fmul_rn(d, d));
+  }
+  q = warp_sum(q);
+  const float var = __fdiv_rn(q, (float)cols);
+  const float inv = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(var, eps)));
+#pragma unroll
+  for (int j = 0; j < PER / VEC; j++) {
+    const int e = (j * 32 + lane) * VEC;
+    Vec<float, VEC> gv = *reinterpret_cast<const Vec<float, VEC>*>(g + e);
+    Vec<float, VEC> bv = *reinterpret_cast<const Vec<float, VEC>*>(b + e);
+    Vec<T, VEC> o;
+#pragma unroll
+    for (int i = 0; i < VEC; i++)
+      o.d[i] = from_f<T>(__fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j * VEC + i], mean), inv), gv.d[i]), bv.d[i]));
+    *reinterpret_cast<Vec<T, VEC>*>(orow + e) = o;
+  }
+}
+
+template <typename T, int PER, int VEC>
+__global__ void __launch_bounds__(128) k_add_ln(const T* __restrict__ x, const T* __restrict__ res, T* out,
+                                                const float* __restrict__ g, const float* __restrict__ b,
+                                                int64_t rows, int cols, float eps) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float v[PER];
+  const T* xr = x + row * cols;
+#pragma unroll
+  for (int j = 0; j < PER / VEC; j++) {
+    const int e = (j * 32 + lane) * VEC;
+    Vec<T, VEC> a = *reinterpret_cast<const Vec<T, VEC>*>(xr + e);
+#pragma unroll
+    for (int i = 0; i < VEC; i++) v[j * VEC + i] = to_f<T>(a.d[i]);
+    if (res) {
+      Vec<T, VEC> r = *reinterpret_cast<const Vec<T, VEC>*>(res + row * cols + e);
+#pragma unroll
+      for (int i = 0; i < VEC; i++) v[j * VEC + i] = __fadd_rn(v[j * VEC + i], to_f<T>(r.d[i]));
+    }
+  }
+  ln_finish<T, PER, VEC>(v, lane, cols, g, b, eps, out + row * cols);
+}
+
+// Fallback for rows that are not a multiple of 32 elements or longer than 1024: one block per
+// row, three passes over global memory.
+template <typename T>
+__global__ void k_add_ln_generic(const T* x, const T* res, T* out, const float* g, const float* b,
+                                 int64_t rows, int cols, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * cols;
+  const T* rr = res ? res + row * cols : nullptr;
+  auto val = [&](int j) { return rr ? __fadd_rn(to_f<T>(xr[j]), to_f<T>(rr[j])) : to_f<T>(xr[j]); };
+  auto block_sum = [&](float s) {
+    s = warp_sum(s);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += red[i];
+    return t;
+  };
+  float s = 0.f;
+  for (int j = threadIdx.x; j < cols; j += blockDim.x) s += val(j);
+  const float mean = __fdiv_rn(block_sum(s), (float)cols);
+  float q = 0.f;
+  for (int j = threadIdx.x; j < cols; j += blockDim.x) {
+    float d = __fsub_rn(val(j), mean);
+    q = __fadd_rn(q, __fmul_rn(d, d));
+  }
+  const float var = __fdiv_rn(block_sum(q), (float)cols);
+  const float inv = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(var, eps)));
+  __syncthreads();
+  for (int j = threadIdx.x; j < cols; j += blockDim.x)
+    out[row * cols + j] = from_f<T>(__fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(val(j), mean), inv), g[j]), b[j]));
+}
+
+template <typename T>
+static int32_t add_ln_t(Ctx* c, const T* x, const T* res, T* out, const float* g, const float* b,
+                        int64_t rows, int64_t cols, float eps) {
+  if (rows == 0) return FLETCHER_OK;
+  const int per = (int)(cols / 32);
+  const int grid = (int)((rows * 32 + 127) / 128);
+  constexpr int V16 = sizeof(T) == 2 ? 8 : 4;
+  bool done = true;
+  if (cols % 32 != 0) done = false;
+#define FL_LN(PER_, VEC_) k_add_ln<T, PER_, VEC_><<<grid, 128, 0, c->stream>>>(x, res, out, g, b, rows, (int)cols, eps)
+  else if (per == 24 && cols % (32 * V16) == 0) FL_LN(24, V16);
+  else if (per == 32 && cols % (32 * V16) == 0) FL_LN(32, V16);
+  else if (per == 16 && cols % (32 * V16) == 0) FL_LN(16, V16);
+  else if (per == 8 && cols % (32 * V16) == 0) FL_LN(8, V16);
+  else if (per == 12 && cols % 128 == 0) FL_LN(12, 4);
+  else if (per == 4 && cols % 128 == 0) FL_LN(4, 4);
+  else if (per == 4) FL_LN(4, 1);
+  else if (per == 2) FL_LN(2, 2);
+  else if (per == 1) FL_LN(1, 1);
+  else done = false;
+#undef FL_LN
+  if (!done) k_add_ln_generic<T><<<(unsigned)rows, 256, 0, c->stream>>>(x, res, out, g, b, rows, (int)cols, eps);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+int32_t launch_add_layernorm(Ctx* c, int32_t dt, const void* x, const void* res, void* out,
+                             const float* g, const float* b, int64_t rows, int64_t cols, float eps) {
+  if (dt == FLETCHER_F32) return add_ln_t<float>(c, (const float*)x, (const float*)res, (float*)out, g, b, rows, cols, eps);
+  if (dt == FLETCHER_BF16)
+    return add_ln_t<__nv_bfloat16>(c, (const __nv_bfloat16*)x, (const __nv_bfloat16*)res, (__nv_bfloat16*)out, g, b, rows, cols, eps);
+  return add_ln_t<__half>(c, (const __half*)x, (const __half*)res, (__half*)out, g, b, rows, cols, eps);
+}
+
+// ---------------------------------------------------------------- embedding
+// bert.go:215-261: word[id] + pos[min(p, P-1)] (absolute only) + type[0], then LayerNorm.
+// The adds happen in the reference's order (word + pos, then + type) in fp32.
+template <typename T, int PER, int VEC>
+__global__ void __launch_bounds__(128) k_embed(const int32_t* __restrict__ ids, const int32_t* __restrict__ pos,
+                                               const T* __restrict__ word, const T* __restrict__ ptab, int max_pos,
+                                               const T* __restrict__ type0, const float* __restrict__ g,
+                                               const float* __restrict__ b, T* __restrict__ out, int64_t rows,
+                                               int cols, float eps) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* wr = word + (int64_t)ids[row] * cols;
+  const T* pr = nullptr;
+  if (ptab) {
+    int p = pos[row];
+    pr = ptab + (int64_t)(p >= max_pos ? max_pos - 1 : p) * cols;
+  }
+  float v[PER];
+#pragma unroll
+  for (int j = 0; j < PER / VEC; j++) {
+    const int e = (j * 32 + lane) * VEC;
+    Vec<T, VEC> a = *reinterpret_cast<const Vec<T, VEC>*>(wr + e);
+    Vec<T, VEC> t = *reinterpret_cast<const Vec<T, VEC>*>(type0 + e);
+#pragma unroll
+    for (int i = 0; i < VEC; i++) v[j * VEC + i] = to_f<T>(a.d[i]);
+    if (pr) {
+      Vec<T, VEC> p = *reinterpret_cast<const Vec<T, VEC>*>(pr + e);
+#pragma unroll
+      for (int i = 0; i < VEC; i++) v[j * VEC + i] = __fadd_rn(v[j * VEC + i], to_f<T>(p.d[i]));
+    }
+#pragma unroll
+    for (int i = 0; i < VEC; i++) v[j * VEC + i] = __fadd_rn(v[j * VEC + i], to_f<T>(t.d[i]));
+  }
+  ln_finish<T, PER, VEC>(v, lane, cols, g, b, eps, out + row * cols);
+}
+
+template <typename T>
+__global__ void k_embed_sum_generic(const int32_t* ids, const int32_t* pos, const T* word, const T* ptab,
+                                    int max_pos, const T* type0, T* out, int64_t rows, int cols) {
+  const int64_t row = blockIdx.x;
+  const T* wr = word + (int64_t)ids[row] * cols;
+  const T* pr = nullptr;
+  if (ptab) {
+    int p = pos[row];
+    pr = ptab + (int64_t)(p >= max_pos ? max_pos - 1 : p) * cols;
+  }
+  for (int j = threadIdx.x; j < cols; j += blockDim.x) {
+    float v = to_f<T>(wr[j]);
+    if (pr) v = __fadd_rn(v, to_f<T>(pr[j]));
+    out[row * cols + j] = from_f<T>(__fadd_rn(v, to_f<T>(type0[j])));
+  }
+}
+
+template <typename T>
+static int32_t embed_t(Ctx* c, const int32_t* ids, const int32_t* pos, const T* word, const T* ptab, int max_pos,
+                       const T* type0, const float* g, const float* b, T* out, int64_t rows, int64_t cols, float eps) {
+  if (rows == 0) return FLETCHER_OK;
+  const int grid = (int)((rows * 32 + 127) / 128);
+  constexpr int V16 = sizeof(T) == 2 ? 8 : 4;
+  const int per = (int)(cols / 32);
+  bool done = cols % 32 == 0;
+#define FL_EM(PER_, VEC_) k_embed<T, PER_, VEC_><<<grid, 128, 0, c->stream>>>(ids, pos, word, ptab, max_pos, type0, g, b, out, rows, (int)cols, eps)
+  if (!done) {
+  } else if (per == 24 && cols % (32 * V16) == 0) FL_EM(24, V16);
+  else if (per == 32 && cols % (32 * V16) == 0) FL_EM(32, V16);
+  else if (per == 16 && cols % (32 * V16) == 0) FL_EM(16, V16);
+  else if (per == 8 && cols % (32 * V16) == 0) FL_EM(8, V16);
+  else if (per == 12 && cols % 128 == 0) FL_EM(12, 4);
+  else if (per == 4 && cols % 128 == 0) FL_EM(4, 4);
+  else if (per == 4) FL_EM(4, 1);
+  else done = false;
+#undef FL_EM
+  if (!done) {
+    k_embed_sum_generic<T><<<(unsigned)rows, 256, 0, c->stream>>>(ids, pos, word, ptab, max_pos, type0, out, rows, (int)cols);
+    FL_LAUNCH(c);
+    return add_ln_t<T>(c, out, nullptr, out, g, b, rows, cols, eps);
+  }
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+int32_t launch_embed(Ctx* c, int32_t dt, const int32_t* ids, const int32_t* pos, const void* word,
+                     const void* ptab, int32_t max_pos, const void* type0, const float* g, const float* b,
+                     void* out, int64_t T, int64_t H, float eps) {
+  if (dt == FLETCHER_F32)
+    return embed_t<float>(c, ids, pos, (const float*)word, (const float*)ptab, max_pos, (const float*)type0, g, b, (float*)out, T, H, eps);
+  if (dt == FLETCHER_BF16)
+    return embed_t<__nv_bfloat16>(c, ids, pos, (const __nv_bfloat16*)word, (const __nv_bfloat16*)ptab, max_pos,
+                                  (const __nv_bfloat16*)type0, g, b, (__nv_bfloat16*)out, T, H, eps);
+  return embed_t<__half>(c, ids, pos, (const __half*)word, (const __half*)ptab, max_pos, (const __half*)type0, g, b,
+                         (__half*)out, T, H, eps);
+}
+
+// ---------------------------------------------------------------- positions
+__global__ void k_positions(const int32_t* __restrict__ cu, int32_t* __restrict__ pos) {
+  const int s = blockIdx.x;
+  const int a = cu[s], e = cu[s + 1];
+  for (int i = a + threadIdx.x; i < e; i += blockDim.x) pos[i] = i - a;
+}
+
+int32_t launch_positions(Ctx* c, const int32_t* cu, int32_t B, int32_t* pos, int32_t) {
+  if (B <= 0) return FLETCHER_OK;
+  k_positions<<<B, 256, 0, c->stream>>>(cu, pos);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+// ---------------------------------------------------------------- mean pool + L2
+// One block per sequence.  Threads split into column groups (VEC columns each, 128-bit loads)
+// and row groups; partial sums meet in shared memory, then the L2 norm is a block reduction.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) k_mean_pool_l2(const T* __restrict__ h, const int32_t* __restrict__ cu,
+                                                      int H, float* __restrict__ out) {
+  extern __shared__ float part[];  // [RG][H]
+  __shared__ float red[8];
+  const int s = blockIdx.x;
+  const int a = cu[s], e = cu[s + 1];
+  const int CG = H / VEC;
+  const bool wide = CG >= (int)blockDim.x;
+  const int RG = wide ? 1 : (int)blockDim.x / CG;
+  const int rg = wide ? 0 : (int)threadIdx.x / CG;
+  if (rg < RG) {
+    for (int cg = wide ? (int)threadIdx.x : (int)threadIdx.x % CG; cg < CG; cg += wide ? (int)blockDim.x : CG) {
+      float acc[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; i++) acc[i] = 0.f;
+      for (int r = a + rg; r < e; r += RG) {
+        Vec<T, VEC> x = *reinterpret_cast<const Vec<T, VEC>*>(h + (int64_t)r * H + cg * VEC);
+#pragma unroll
+        for (int i = 0; i < VEC; i++) acc[i] += to_f<T>(x.d[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < VEC; i++) part[rg * H + cg * VEC + i] = acc[i];
+    }
+  }
+  __syncthreads();
+  const float invn = e > a ? 1.0f / (float)(e - a) : 0.f;
+  float sq = 0.f;
+  for (int j = threadIdx.x; j < H; j += blockDim.x) {
+    float t = 0.f;
+    for (int g = 0; g < RG; g++) t += part[g * H + j];
+    t *= invn;
+    part[j] = t;  // row group 0 slot now holds the mean (only this thread touches column j)
+    sq += t * t;
+  }
+  sq = warp_sum(sq);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += red[i];
+  const float inv = tot > 0.f ? (float)(1.0 / sqrt((double)tot)) : 0.f;
+  for (int j = threadIdx.x; j < H; j += blockDim.x) out[(int64_t)s * H + j] = part[j] * inv;
+}
+
+template <typename T>
+static int32_t mean_pool_t(Ctx* c, const T* h, const int32_t* cu, int B, int64_t H, float* out) {
+  constexpr int V = sizeof(T) == 2 ? 8 : 4;
+  const bool vec = H % V == 0 && H / V <= 256;
+  if (B <= 0) return FLETCHER_OK;
+  if (vec) {
+    const int CG = (int)(H / V);
+    const int RG = 256 / CG;
+    k_mean_pool_l2<T, V><<<B, 256, (size_t)RG * H * 4, c->stream>>>(h, cu, (int)H, out);
+  } else {
+    FL_CHECK(c, H <= 16384, "MeanPoolL2: hidden %lld too large", (long long)H);
+    k_mean_pool_l2<T, 1><<<B, 256, (size_t)(H < 256 ? 256 / H : 1) * H * 4, c->stream>>>(h, cu, (int)H, out);
+  }
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+int32_t launch_mean_pool_l2(Ctx* c, int32_t dt, const void* h, const int32_t* cu, int32_t B, int64_t H, float* out) {
+  if (dt == FLETCHER_F32) return mean_pool_t<float>(c, (const float*)h, cu, B, H, out);
+  if (dt == FLETCHER_BF16) return mean_pool_t<__nv_bfloat16>(c, (const __nv_bfloat16*)h, cu, B, H, out);
+  return mean_pool_t<__half>(c, (const __half*)h, cu, B, H, out);
+}
+
+// ---------------------------------------------------------------- gather rows -> f32
+template <typename T>
+__global__ void k_gather_rows_f32(const T* __restrict__ src, const int32_t* __restrict__ idx, int64_t H,
+                                  float* __restrict__ dst) {
+  const int64_t i = blockIdx.x;
+  const T* s = src + (int64_t)idx[i] * H;
+  for (int64_t j = threadIdx.x; j < H; j += blockDim.x) dst[i * H + j] = to_f<T>(s[j]);
+}
+
+int32_t launch_gather_rows_f32(Ctx* c, int32_t dt, const void* src, const int32_t* idx, int64_t n, int64_t H, float* dst) {
+  if (n <= 0) return FLETCHER_OK;
+  if (dt == FLETCHER_F32) k_gather_rows_f32<float><<<(unsigned)n, 256, 0, c->stream>>>((const float*)src, idx, H, dst);
+  else if (dt == FLETCHER_BF16) k_gather_rows_f32<__nv_bfloat16><<<(unsigned)n, 256, 0, c->stream>>>((const __nv_bfloat16*)src, idx, H, dst);
+  else k_gather_rows_f32<__half><<<(unsigned)n, 256, 0, c->stream>>>((const __half*)src, idx, H, dst);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+// ---------------------------------------------------------------- RoPE
+// cpu_backend.go:789-798: theta = pos * base^(-2i/dh) in float64, cos/sin rounded to float32,
+// then (x1, x2) <- (x1*c - x2*s, x1*s + x2*c) in float32.
+__global__ void k_rope_table(float* cos_t, float* sin_t, int len, int half, int dh, double base) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= (int64_t)len * half) return;
+  const int p = (int)(i / half), k = (int)(i % half);
+  const double theta = (double)p * pow(base, -2.0 * (double)k / (double)dh);
+  cos_t[i] = (float)cos(theta);
+  sin_t[i] = (float)sin(theta);
+}
+
+int32_t launch_rope_build_table(Ctx* c, float* cos_t, float* sin_t, int32_t len, int32_t dh, double base) {
+  const int64_t n = (int64_t)len * (dh / 2);
+  k_rope_table<<<(unsigned)((n + 255) / 256), 256, 0, c->stream>>>(cos_t, sin_t, len, dh / 2, dh, base);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+template <typename T>
+__global__ void k_rope_apply(T* x, int64_t T_, int64_t ld, int64_t ncols, int dh, const int32_t* __restrict__ pos,
+                             const float* __restrict__ ct, const float* __restrict__ st) {
+  const int half = dh / 2;
+  const int64_t per_row = ncols / 2;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= T_ * per_row) return;
+  const int64_t r = i / per_row;
+  const int64_t q = i % per_row;
+  const int64_t head = q / half;
+  const int k = (int)(q % half);
+  T* p = x + r * ld + head * dh;
+  const float cs = ct[(int64_t)pos[r] * half + k], sn = st[(int64_t)pos[r] * half + k];
+  const float x1 = to_f<T>(p[k]), x2 = to_f<T>(p[k + half]);
+  p[k] = from_f<T>(__fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn)));
+  p[k + half] = from_f<T>(__fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs)));
+}
+
+int32_t launch_rope_table(Ctx* c, int32_t dt, void* x, int64_t T, int64_t ld, int64_t ncols, int32_t dh,
+                          const int32_t* pos, const float* ct, const float* st) {
+  const int64_t n = T * (ncols / 2);
+  if (n <= 0) return FLETCHER_OK;
+  const unsigned g = (unsigned)((n + 255) / 256);
+  if (dt == FLETCHER_F32) k_rope_apply<float><<<g, 256, 0, c->stream>>>((float*)x, T, ld, ncols, dh, pos, ct, st);
+  else if (dt == FLETCHER_BF16) k_rope_apply<__nv_bfloat16><<<g, 256, 0, c->stream>>>((__nv_bfloat16*)x, T, ld, ncols, dh, pos, ct, st);
+  else k_rope_apply<__half><<<g, 256, 0, c->stream>>>((__half*)x, T, ld, ncols, dh, pos, ct, st);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+// ---------------------------------------------------------------- SwiGLU (cpu_backend.go:636-654)
+template <typename T>
+__global__ void k_swiglu(const T* __restrict__ in, T* __restrict__ out, int64_t rows, int64_t I) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows * I; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / I, j = i % I;
+    out[i] = from_f<T>(swiglu_exact(to_f<T>(in[r * 2 * I + j]), to_f<T>(in[r * 2 * I + j + I])));
+  }
+}
+
+int32_t launch_swiglu(Ctx* c, int32_t dt, const void* in, void* out, int64_t rows, int64_t I) {
+  const int g = grid_for(rows * I, 256);
+  if (dt == FLETCHER_F32) k_swiglu<float><<<g, 256, 0, c->stream>>>((const float*)in, (float*)out, rows, I);
+  else if (dt == FLETCHER_BF16) k_swiglu<__nv_bfloat16><<<g, 256, 0, c->stream>>>((const __nv_bfloat16*)in, (__nv_bfloat16*)out, rows, I);
+  else k_swiglu<__half><<<g, 256, 0, c->stream>>>((const __half*)in, (__half*)out, rows, I);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+// ---------------------------------------------------------------- elementwise
+template <typename T>
+__global__ void k_scale_add(T* x, const T* other, float scale, float add, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = to_f<T>(x[i]);
+    if (scale != 1.0f) v = __fmul_rn(v, scale);
+    if (add != 0.0f) v = __fadd_rn(v, add);
+    if (other) v = __fadd_rn(v, to_f<T>(other[i]));
+    x[i] = from_f<T>(v);
+  }
+}
+int32_t launch_scale_add(Ctx* c, int32_t dt, void* x, const void* other, float scale, float add, int64_t n) {
+  const int g = grid_for(n, 256);
+  if (n <= 0) return FLETCHER_OK;
+  if (dt == FLETCHER_F32) k_scale_add<float><<<g, 256, 0, c->stream>>>((float*)x, (const float*)other, scale, add, n);
+  else if (dt == FLETCHER_BF16) k_scale_add<__nv_bfloat16><<<g, 256, 0, c->stream>>>((__nv_bfloat16*)x, (const __nv_bfloat16*)other, scale, add, n);
+  else k_scale_add<__half><<<g, 256, 0, c->stream>>>((__half*)x, (const __half*)other, scale, add, n);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+template <typename T>
+__global__ void k_add_bias(T* x, const T* b, int64_t rows, int64_t cols) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows * cols; i += (int64_t)gridDim.x * blockDim.x)
+    x[i] = from_f<T>(__fadd_rn(to_f<T>(x[i]), to_f<T>(b[i % cols])));
+}
+int32_t launch_add_bias(Ctx* c, int32_t dt, void* x, const void* b, int64_t rows, int64_t cols) {
+  const int g = grid_for(rows * cols, 256);
+  if (rows * cols <= 0) return FLETCHER_OK;
+  if (dt == FLETCHER_F32) k_add_bias<float><<<g, 256, 0, c->stream>>>((float*)x, (const float*)b, rows, cols);
+  else if (dt == FLETCHER_BF16) k_add_bias<__nv_bfloat16><<<g, 256, 0, c->stream>>>((__nv_bfloat16*)x, (const __nv_bfloat16*)b, rows, cols);
+  else k_add_bias<__half><<<g, 256, 0, c->stream>>>((__half*)x, (const __half*)b, rows, cols);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+// Softmax rows (SoftmaxFast, simd.go:78-99), one warp per row.
+template <typename T>
+__global__ void k_softmax_rows(T* x, int64_t rows, int64_t cols) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  T* r = x + row * cols;
+  float m = -INFINITY;
+  for (int64_t j = lane; j < cols; j += 32) m = fmaxf(m, to_f<T>(r[j]));
+  m = warp_max(m);
+  float s = 0.f;
+  for (int64_t j = lane; j < cols; j += 32) s += exp_fast(__fsub_rn(to_f<T>(r[j]), m));
+  s = warp_sum(s);
+  const float inv = __fdiv_rn(1.0f, s);
+  for (int64_t j = lane; j < cols; j += 32) r[j] = from_f<T>(__fmul_rn(exp_fast(__fsub_rn(to_f<T>(r[j]), m)), inv));
+}
+
+template <typename T>
+__global__ void k_act(T* x, int64_t n, int32_t act) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = to_f<T>(x[i]);
+    v = act == FLETCHER_ACT_GELU ? gelu_fast(v) : act == FLETCHER_ACT_TANH ? tanh_fast(v) : v;
+    x[i] = from_f<T>(v);
+  }
+}
+
+int32_t launch_activation(Ctx* c, int32_t dt, void* x, int64_t rows, int64_t cols, int32_t act) {
+  if (rows * cols <= 0 || act == FLETCHER_ACT_IDENTITY) return FLETCHER_OK;
+  if (act == FLETCHER_ACT_SOFTMAX) {
+    const unsigned g = (unsigned)((rows * 32 + 255) / 256);
+    if (dt == FLETCHER_F32) k_softmax_rows<float><<<g, 256, 0, c->stream>>>((float*)x, rows, cols);
+    else if (dt == FLETCHER_BF16) k_softmax_rows<__nv_bfloat16><<<g, 256, 0, c->stream>>>((__nv_bfloat16*)x, rows, cols);
+    else k_softmax_rows<__half><<<g, 256, 0, c->stream>>>((__half*)x, rows, cols);
+  } else {
+    FL_CHECK(c, act == FLETCHER_ACT_GELU || act == FLETCHER_ACT_TANH, "Activation: unsupported code %d", act);
+    const int g = grid_for(rows * cols, 256);
+    if (dt == FLETCHER_F32) k_act<float><<<g, 256, 0, c->stream>>>((float*)x, rows * cols, act);
+    else if (dt == FLETCHER_BF16) k_act<__nv_bfloat16><<<g, 256, 0, c->stream>>>((__nv_bfloat16*)x, rows * cols, act);
+    else k_act<__half><<<g, 256, 0, c->stream>>>((__half*)x, rows * cols, act);
+  }
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+template <typename T>
+__global__ void k_has_nan(const T* x, int64_t n, int32_t* flag) {
+  bool bad = false;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    bad |= !isfinite(to_f<T>(x[i]));
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1);
+}
+int32_t launch_has_nan(Ctx* c, int32_t dt, const void* x, int64_t n, int32_t* flag) {
+  if (n <= 0) return FLETCHER_OK;
+  const int g = grid_for(n, 256, 4 * c->num_sms);
+  if (dt == FLETCHER_F32) k_has_nan<float><<<g, 256, 0, c->stream>>>((const float*)x, n, flag);
+  else if (dt == FLETCHER_BF16) k_has_nan<__nv_bfloat16><<<g, 256, 0, c->stream>>>((const __nv_bfloat16*)x, n, flag);
+  else k_has_nan<__half><<<g, 256, 0, c->stream>>>((const __half*)x, n, flag);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+template <typename S, typename D>
+__global__ void k_cast(const S* s, D* d, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    d[i] = from_f<D>(to_f<S>(s[i]));
+}
+template <typename S>
+static void cast_to(Ctx* c, const S* s, int32_t ddt, void* d, int64_t n, int g) {
+  if (ddt == FLETCHER_F32) k_cast<S, float><<<g, 256, 0, c->stream>>>(s, (float*)d, n);
+  else if (ddt == FLETCHER_BF16) k_cast<S, __nv_bfloat16><<<g, 256, 0, c->stream>>>(s, (__nv_bfloat16*)d, n);
+  else k_cast<S, __half><<<g, 256, 0, c->stream>>>(s, (__half*)d, n);
+}
+int32_t launch_cast(Ctx* c, int32_t sdt, const void* s, int32_t ddt, void* d, int64_t n) {
+  if (n <= 0) return FLETCHER_OK;
+  const int g = grid_for(n, 256);
+  if (sdt == FLETCHER_F32) cast_to<float>(c, (const float*)s, ddt, d, n, g);
+  else if (sdt == FLETCHER_BF16) cast_to<__nv_bfloat16>(c, (const __nv_bfloat16*)s, ddt, d, n, g);
+  else cast_to<__half>(c, (const __half*)s, ddt, d, n, g);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+// ---------------------------------------------------------------- weight packing
+// dst[n', k] = src[k, col(n')]: (in,out) fp32 -> K-major 16-bit for the tensor-core GEMM.
+// perm 1 interleaves a SwiGLU [gate | up] weight so that every block_n-row tile holds
+// block_n/2 gate rows followed by the matching block_n/2 up rows.
+__device__ __forceinline__ int64_t packed_src_col(int64_t n, int64_t N, int perm, int block_n) {
+  if (perm == 0) return n;
+  const int64_t half = block_n / 2, I = N / 2;
+  const int64_t j = n / block_n, r = n % block_n;
+  return r < half ? j * half + r : I + j * half + (r - half);
+}
+
+template <typename S, typename T>
+__global__ void k_pack_kmajor(const S* __restrict__ src, int64_t K, int64_t N, T* __restrict__ dst, int perm,
+                              int block_n) {
+  __shared__ float tile[32][33];
+  const int64_t k0 = (int64_t)blockIdx.x * 32, n0 = (int64_t)blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t k = k0 + i, n = n0 + threadIdx.x;
+    tile[i][threadIdx.x] = (k < K && n < N) ? to_f<S>(src[k * N + packed_src_col(n, N, perm, block_n)]) : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t n = n0 + i, k = k0 + threadIdx.x;
+    if (n < N && k < K) dst[n * K + k] = from_f<T>(tile[threadIdx.x][i]);
+  }
+}
+
+int32_t launch_pack_weight_kmajor(Ctx* c, const float* src, int64_t K, int64_t N, void* dst, int32_t dt,
+                                  int32_t perm, int32_t block_n) {
+  dim3 grid((unsigned)((K + 31) / 32), (unsigned)((N + 31) / 32)), blk(32, 8);
+  if (dt == FLETCHER_BF16) k_pack_kmajor<float, __nv_bfloat16><<<grid, blk, 0, c->stream>>>(src, K, N, (__nv_bfloat16*)dst, perm, block_n);
+  else if (dt == FLETCHER_F16) k_pack_kmajor<float, __half><<<grid, blk, 0, c->stream>>>(src, K, N, (__half*)dst, perm, block_n);
+  else k_pack_kmajor<float, float><<<grid, blk, 0, c->stream>>>(src, K, N, (float*)dst, perm, block_n);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+int32_t launch_pack_kmajor_16(Ctx* c, int32_t dt, const void* src, int64_t K, int64_t N, void* dst, int32_t perm,
+                              int32_t block_n) {
+  dim3 grid((unsigned)((K + 31) / 32), (unsigned)((N + 31) / 32)), blk(32, 8);
+  if (dt == FLETCHER_BF16)
+    k_pack_kmajor<__nv_bfloat16, __nv_bfloat16><<<grid, blk, 0, c->stream>>>((const __nv_bfloat16*)src, K, N, (__nv_bfloat16*)dst, perm, block_n);
+  else
+    k_pack_kmajor<__half, __half><<<grid, blk, 0, c->stream>>>((const __half*)src, K, N, (__half*)dst, perm, block_n);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+}  // namespace fl

@@ -1,0 +1,122 @@
+"""GPU parity of the whole forward pass (Cuda_Model_*) against the CPU oracle and its golden
+fixtures.  fp32: per-vector cosine >= 0.99999 and max-abs <= 1e-4; bf16/fp16: cosine >= 0.999."""
+import dataclasses
+
+import numpy as np
+import pytest
+
+import synth
+from helpers import assert_close_16, assert_close_f32, load_golden
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = ["tiny_ragged_spec", "tiny_uniform_literal", "nomic2_ragged_spec", "nomic2_uniform_literal"]
+
+
+@pytest.fixture(scope="module")
+def be():
+    import build
+    build.build()
+    import fletcher
+    b = fletcher.Backend(0)
+    yield b
+
+
+_models = {}
+
+
+def model(be, cfg, dtype, seed):
+    import fletcher
+    key = (cfg, dtype, seed)
+    if key not in _models:
+        m = fletcher.BertModel(be, cfg, dtype)
+        m.load_raw(synth.make_weights(cfg, seed))
+        _models[key] = m
+    return _models[key]
+
+
+@pytest.mark.parametrize("name", GOLDEN)
+@pytest.mark.parametrize("pooling", [0, 1])
+def test_f32_matches_golden(be, name, pooling):
+    cfg, g = load_golden(name)
+    m = model(be, cfg, "f32", int(g["weight_seed"]))
+    got = m.forward_batch(g["ids"], g["lengths"], pooling)
+    assert_close_f32(got, g["mean" if pooling == 1 else "cls"], f"{name} pooling={pooling}")
+
+
+@pytest.mark.parametrize("name", GOLDEN)
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_16bit_matches_golden(be, name, dtype):
+    cfg, g = load_golden(name)
+    m = model(be, cfg, dtype, int(g["weight_seed"]))
+    for pooling, key in ((1, "mean"), (0, "cls")):
+        got = m.forward_batch(g["ids"], g["lengths"], pooling)
+        assert_close_16(got, g[key], f"{name} {dtype} {key}")
+
+
+def test_cfg1_full_batch_f32(be, oracle_mod):
+    w = synth.WORKLOADS["cfg1"]
+    lens = w.lengths()
+    ids = synth.make_ids(lens, w.cfg.vocab_size, w.seed)
+    blob = synth.make_weights(w.cfg, w.seed)
+    want = oracle_mod.forward(w.cfg, blob, ids, lens)
+    m = model(be, w.cfg, "f32", w.seed)
+    assert_close_f32(m.forward_batch(ids, lens, 1), want["mean"], "cfg1 mean")
+    assert_close_f32(m.forward_batch(ids, lens, 0), want["cls"], "cfg1 cls")
+
+
+@pytest.mark.parametrize("lengths", [[1], [2, 1, 3], [63, 64, 65], [127, 128, 129, 1], [300, 17]])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_edge_lengths_nomic(be, oracle_mod, lengths, dtype):
+    cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
+    lens = np.array(lengths, np.int32)
+    ids = synth.make_ids(lens, cfg.vocab_size, 21)
+    blob = synth.make_weights(cfg, 1)
+    want = oracle_mod.forward(cfg, blob, ids, lens)
+    got = model(be, cfg, dtype, 1).forward_batch(ids, lens, 1)
+    (assert_close_f32 if dtype == "f32" else assert_close_16)(got, want["mean"], f"{dtype} {lengths}")
+
+
+def test_packing_invariance_bitexact(be):
+    """A sequence's embedding does not depend on the other sequences packed with it."""
+    cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
+    m = model(be, cfg, "bf16", 1)
+    lens = np.array([200, 5, 64, 129, 31], np.int32)
+    ids = synth.make_ids(lens, cfg.vocab_size, 9)
+    full = m.forward_batch(ids, lens, 1)
+    off = 0
+    for i, L in enumerate(lens):
+        single = m.forward_batch(ids[off:off + L], lens[i:i + 1], 1)
+        assert np.array_equal(single[0], full[i]), i
+        off += L
+
+
+def test_cfg3_full_size_bf16(be, oracle_mod):
+    """BASELINE cfg3 at full size (12 layers, B=256, l in [32,512]): finite unit vectors,
+    and a sample of sequences against the oracle."""
+    w = synth.WORKLOADS["cfg3"]
+    lens = w.lengths()
+    ids = synth.make_ids(lens, w.cfg.vocab_size, w.seed)
+    blob = synth.make_weights(w.cfg, w.seed)
+    m = model(be, w.cfg, "bf16", w.seed)
+    got = m.forward_batch(ids, lens, 1)
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(np.linalg.norm(got, axis=1), 1.0, atol=1e-4)
+    starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    pick = np.argsort(lens)[[0, 1, len(lens) // 2, -1]]
+    for i in pick:
+        want = oracle_mod.forward(w.cfg, blob, ids[starts[i]:starts[i] + lens[i]], lens[i:i + 1])
+        assert_close_16(got[i:i + 1], want["mean"], f"cfg3 seq {i} len {lens[i]}")
+
+
+def test_errors_are_reported(be):
+    import fletcher
+    cfg = synth.BERT_TINY
+    m = fletcher.BertModel(be, cfg, "f32")
+    with pytest.raises(fletcher.FletcherError):
+        m.load_raw(np.zeros(10, np.float32))
+    m.load_raw(synth.make_weights(cfg, 0))
+    with pytest.raises(fletcher.FletcherError) as e:
+        m.forward_batch(np.array([101, 99999, 102], np.int32), np.array([3], np.int32))
+    assert "out of bounds" in str(e.value)
+    m.close()
