@@ -1,0 +1,302 @@
+#!/usr/bin/env python
+"""Benchmark of the embedding forward pass (BertModel.ForwardBatch, bert.go:149-169) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fletcher|reference] [--workload cfg3]
+
+One step = one forward pass of one batch of the workload (default cfg3: nomic-embed-text
+architecture, bf16, B=256 sequences per GPU, lengths U[32,512], packed varlen) through
+libcuda_fletcher.so.  With N>1 (launched by torchrun) every rank runs an independent replica on
+its own batches (weak scaling); no collective touches the data path — torch.distributed is only
+used for the barrier and the max-over-ranks of the device time.
+
+Printed (rank 0, one JSON line):
+  value     vectors/s over all ranks, inputs resident in HBM, device time of K steps (CUDA
+            events on the library's stream), max over ranks;
+  e2e       the same metric through the public host entry point Cuda_Model_ForwardBatch with
+            pinned host ids in and host vectors out (H2D + D2H inside the timed region);
+  roofline  the tensor-core GEMMs (the dominant kernels): algorithmic FLOPs / their event-timed
+            duration, against the measured sustained bf16 peak;
+  cpu_baseline  the CPU oracle (C++ restatement of the reference's CPU path, OpenBLAS sgemm)
+            on a bounded sample of the same workload, all host cores (rank 0, N=1 only).
+--impl reference times that CPU implementation alone as the reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "longbow-fletcher_b200")]
+import synth  # noqa: E402
+
+METRIC = "embeddings/sec (nomic-embed-text seq512 bf16)"
+# ncu-measured DRAM traffic per launch of the tensor-core GEMMs (profiles/gemm_tc_cfg3.md),
+# bytes per launch, keyed by stage; None until captured.
+GEMM_TRAFFIC = None
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["bf16_tflops_sustained"], d["bf16_tflops"], d["hbm_gbs"], "measured"
+    return 1400.0, 1590.0, 6650.0, "fallback"
+
+
+class Clocks:
+    """Samples nvidia-smi SM clocks and throttle reasons while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            self.p.wait()
+
+    def summary(self):
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                "samples": len(rows), "reasons": reasons}
+
+
+def make_batches(w, n, rank, seed_base):
+    out = []
+    for i in range(n):
+        seed = seed_base + 1000 * rank + i
+        lens = synth.make_lengths(w.batch, w.len_lo, w.len_hi, seed, w.dist)
+        ids = synth.make_ids(lens, w.cfg.vocab_size, seed)
+        out.append((ids, lens))
+    return out
+
+
+def cpu_reference(w, steps, warmup, sample, threads):
+    """Times the CPU oracle on `sample` sequences per step.  Returns vectors/s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    blob = synth.make_weights(w.cfg, w.seed)
+    oracle.lib(threads)
+    batches = []
+    for i in range(warmup + steps):
+        lens = synth.make_lengths(sample, w.len_lo, w.len_hi, 7000 + i, w.dist)
+        batches.append((synth.make_ids(lens, w.cfg.vocab_size, 7000 + i), lens))
+    for ids, lens in batches[:warmup]:
+        oracle.forward(w.cfg, blob, ids, lens, mode=oracle.MODE_SPEC)
+    t0 = time.perf_counter()
+    for ids, lens in batches[warmup:]:
+        oracle.forward(w.cfg, blob, ids, lens, mode=oracle.MODE_SPEC)
+    dt = time.perf_counter() - t0
+    return steps * sample / dt, dt
+
+
+def run_reference(args, w, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    v, dt = cpu_reference(w, args.steps, args.warmup, args.ref_sample, threads)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "vectors/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w.name, "batch_per_step": args.ref_sample, "seq_len": w.len_hi},
+        "cpu_baseline": {"value": v, "unit": "vectors/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.ref_sample} sequences per step from the {w.name} length distribution; "
+                                   "C++ restatement of the reference CPU path (Go + OpenBLAS is not buildable here)"},
+        "e2e": {"value": v, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="fletcher", choices=["fletcher", "reference"])
+    ap.add_argument("--workload", default="cfg3", choices=sorted(synth.WORKLOADS))
+    ap.add_argument("--ref-sample", type=int, default=4, help="sequences per step for the CPU reference")
+    ap.add_argument("--cpu-sample", type=int, default=8, help="sequences in the cpu_baseline sample")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    w = synth.WORKLOADS[args.workload]
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, w, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    import fletcher as fl
+
+    be = fl.Backend(local, w.dtype)
+    model = fl.BertModel(be, w.cfg, w.dtype)
+    model.load_raw(synth.make_weights(w.cfg, w.seed))
+    stream = torch.cuda.ExternalStream(be.stream(), device=torch.device("cuda", local))
+
+    nb = 4
+    batches = make_batches(w, nb, rank, 500)
+    d_ids = [torch.from_numpy(ids).to(f"cuda:{local}") for ids, _ in batches]
+    H = w.cfg.hidden
+    d_out = torch.empty((w.batch, H), dtype=torch.float32, device=f"cuda:{local}")
+    torch.cuda.synchronize()
+
+    def step(i):
+        ids, lens = batches[i % nb]
+        model.forward_batch_device(d_ids[i % nb].data_ptr(), lens, fl.POOL_MEAN_L2, d_out.data_ptr())
+
+    for i in range(args.warmup):
+        step(i)
+    be.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident timing
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    l0 = be.launch_count()
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        e1.synchronize()
+    be.synchronize()
+    launches = be.launch_count() - l0
+    barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    seqs = sum(len(batches[i % nb][1]) for i in range(args.steps))
+    tokens = sum(int(batches[i % nb][1].sum()) for i in range(args.steps))
+    flops = sum(float(w.cfg.flops_per_sequence(batches[i % nb][1]).sum()) for i in range(args.steps))
+    value = seqs * world / (ms_max / 1000)
+
+    # ---- per-stage timing pass (events around every stage, separate from the timed region)
+    model.set_stage_timing(True)
+    ns = min(args.steps, 5)
+    for i in range(ns):
+        step(i)
+    st = model.stage_times()
+    model.set_stage_timing(False)
+    cfg = w.cfg
+    Hh, I, Iu, L = cfg.hidden, cfg.intermediate, cfg.up_width, cfg.num_layers
+    gemm_stages = ["gemm_qkv", "gemm_o", "gemm_up", "gemm_down"]
+    tok_ns = sum(int(batches[i % nb][1].sum()) for i in range(ns))
+    gemm_flops = 2.0 * tok_ns * L * (Hh * 3 * Hh + Hh * Hh + Hh * Iu + I * Hh)
+    gemm_ms = sum(st[s][0] for s in gemm_stages)
+    gemm_launches = sum(st[s][1] for s in gemm_stages)
+    sustained, burst, hbm, src = peaks()
+    achieved = gemm_flops / gemm_launches / (gemm_ms / gemm_launches / 1000) / 1e12
+    roofline = {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05, all 4 GEMMs of every layer)",
+                "achieved": achieved, "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
+                "peak_source": f"{src} bf16_tflops_sustained", "traffic": GEMM_TRAFFIC,
+                "flops_per_launch": gemm_flops / gemm_launches, "ms_per_launch": gemm_ms / gemm_launches}
+    stage_ms = {k: v[0] / ns for k, v in st.items() if v[1]}
+
+    # ---- end to end through the host entry point (pinned host buffers)
+    pin_ids = [torch.from_numpy(ids).pin_memory().numpy() for ids, _ in batches]
+    out_host = torch.empty((w.batch, H), dtype=torch.float32).pin_memory().numpy()
+    import ctypes
+    lib = fl.lib()
+
+    def e2e_step(i):
+        ids, lens = batches[i % nb]
+        lens = np.ascontiguousarray(lens, np.int32)
+        be.check(lib.Cuda_Model_ForwardBatch(model.h, fl._i32p(pin_ids[i % nb]), fl._i32p(lens), lens.size,
+                                             fl.POOL_MEAN_L2, out_host.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+
+    for i in range(2):
+        e2e_step(i)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    e1.synchronize()
+    wall = time.perf_counter() - t0
+    e2e_ms = max(e0.elapsed_time(e1), wall * 1000)
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = seqs * world / (float(t.item()) / 1000)
+    h2d = tokens * 4 // args.steps
+    d2h = w.batch * H * 4
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, dt = cpu_reference(w, 1, 1, args.cpu_sample, os.cpu_count() or 1)
+        cpu = {"value": v, "unit": "vectors/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"1 timed step of {args.cpu_sample} sequences from the {w.name} length distribution "
+                         f"({dt:.1f} s), spec mode, OpenBLAS sgemm + the reference's scalar loops"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "vectors/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+            "config": {"workload": f"{args.workload}: {w.name}, lengths {w.dist} [{w.len_lo},{w.len_hi}], packed varlen, "
+                                   "mean pool + L2", "global_batch": w.batch * world, "seq_len": w.len_hi,
+                       "parallelism": f"replicas x{world} (no collective)",
+                       "l2": "inputs larger than L2: 0.27 GB weights + ~1 GB activations streamed per step"},
+            "tokens_per_step": tokens / args.steps,
+            "model_tflops": flops * world / (ms_max / 1000) / 1e12,
+            "roofline": roofline,
+            "stage_ms_per_step": stage_ms,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "vectors/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

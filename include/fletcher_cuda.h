@@ -96,6 +96,8 @@ int32_t Cuda_GetLastError(CudaContextRef ctx, char* buf, int32_t len);
 int32_t Cuda_Synchronize(CudaContextRef ctx);
 /* The context's cudaStream_t, for callers that time or order work around it. */
 void* Cuda_GetStream(CudaContextRef ctx);
+/* Number of kernels this context has launched so far (for launch accounting). */
+int64_t Cuda_GetLaunchCount(CudaContextRef ctx);
 /* device.Backend.GetVRAMUsage (device.go:161): bytes held by this context's buffers, and
  * the device's total memory. */
 int32_t Cuda_MemGetInfo(CudaContextRef ctx, int64_t* allocated, int64_t* total);
@@ -198,6 +200,25 @@ int32_t Cuda_Model_ForwardBatch(CudaModelRef model, const int32_t* ids, const in
 int32_t Cuda_Model_ForwardBatchDevice(CudaModelRef model, const int32_t* d_ids,
                                       const int32_t* lengths, int32_t numSeqs, int32_t pooling,
                                       float* d_out);
+/* Stage timing: when enabled, every stage of the forward pass is bracketed by CUDA events on
+ * the context's stream.  Cuda_Model_StageTimes synchronises, writes the summed milliseconds
+ * (and the number of timed calls) per stage since the last read into ms[n] / launches[n]
+ * (launches may be NULL), then resets.  Stage indices: */
+enum {
+  FLETCHER_STAGE_EMBED = 0,
+  FLETCHER_STAGE_GEMM_QKV = 1,
+  FLETCHER_STAGE_ROPE = 2,
+  FLETCHER_STAGE_ATTENTION = 3,
+  FLETCHER_STAGE_GEMM_O = 4,
+  FLETCHER_STAGE_LAYERNORM = 5,
+  FLETCHER_STAGE_GEMM_UP = 6,
+  FLETCHER_STAGE_ACTIVATION = 7,
+  FLETCHER_STAGE_GEMM_DOWN = 8,
+  FLETCHER_STAGE_POOL = 9,
+  FLETCHER_NUM_STAGES = 10
+};
+int32_t Cuda_Model_SetStageTiming(CudaModelRef model, int32_t enable);
+int32_t Cuda_Model_StageTimes(CudaModelRef model, float* ms, int64_t* launches, int32_t n);
 /* Copies the last hidden state [sum(lengths), hidden] of the previous forward as float32. */
 int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count);
 int32_t Cuda_Model_Free(CudaModelRef model);

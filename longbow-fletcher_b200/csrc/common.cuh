@@ -22,6 +22,7 @@ struct Ctx {
   int num_sms = 148;
   int64_t allocated = 0;
   int32_t* d_err = nullptr;  // device flag, set by kernels on a bounded-wait timeout
+  int64_t launches = 0;      // kernels launched on this context (counted by FL_LAUNCH)
   std::string last_error;
 };
 
@@ -57,6 +58,7 @@ struct DeviceGuard {
 
 #define FL_LAUNCH(ctx)                                                                      \
   do {                                                                                      \
+    (ctx)->launches++;                                                                      \
     cudaError_t e_ = cudaGetLastError();                                                    \
     if (e_ != cudaSuccess)                                                                  \
       return ::fl::set_error((ctx), FLETCHER_ERR_CUDA, "kernel launch failed: %s (%s:%d)",  \

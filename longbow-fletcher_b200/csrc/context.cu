@@ -36,7 +36,7 @@ int32_t dev_alloc(Ctx* c, void** p, int64_t bytes) {
 void dev_free(Ctx* c, void* p, int64_t bytes) {
   if (!p) return;
   cudaFreeAsync(p, c->stream);
-  c->allocated -= bytes;
+  c->allocated -= bytes <= 0 ? 16 : bytes;  // mirrors the minimum size dev_alloc charges
 }
 
 static int32_t init_on_device(Ctx* c, int device) {
@@ -186,6 +186,8 @@ int32_t Cuda_Synchronize(CudaContextRef ctx) {
 
 void* Cuda_GetStream(CudaContextRef ctx) { return ctx ? (void*)C(ctx)->stream : nullptr; }
 
+int64_t Cuda_GetLaunchCount(CudaContextRef ctx) { return ctx ? C(ctx)->launches : -1; }
+
 int32_t Cuda_MemGetInfo(CudaContextRef ctx, int64_t* allocated, int64_t* total) {
   Ctx* c = C(ctx);
   if (!c) return FLETCHER_ERR_INVALID;
@@ -224,7 +226,7 @@ int32_t Cuda_FreeBuffer(CudaContextRef ctx, CudaBufferRef buf) {
   if (!b) return FLETCHER_OK;
   Ctx* c = ctx ? C(ctx) : b->ctx;
   DeviceGuard g(c);
-  dev_free(c, b->ptr, b->bytes < 16 ? 16 : b->bytes);
+  dev_free(c, b->ptr, b->bytes);
   delete b;
   return FLETCHER_OK;
 }

@@ -66,6 +66,15 @@ struct Model {
   int64_t h_meta_cap = 0;
   cudaEvent_t meta_done = nullptr;
   int64_t last_T = 0;
+  // stage timing
+  bool timing = false;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  struct StageRec {
+    int cat;
+    cudaEvent_t a, b;
+  };
+  std::vector<StageRec> stage_recs;
 };
 
 static int32_t own(Model* m, void** p, int64_t bytes) {
@@ -316,6 +325,32 @@ static int32_t upload_meta(Model* m, const int32_t* lengths, int32_t B, int64_t 
   return FLETCHER_OK;
 }
 
+// ---- optional per-stage timing with CUDA events on the context's stream
+static cudaEvent_t next_event(Model* m) {
+  if (m->ev_used == m->ev_pool.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    m->ev_pool.push_back(e);
+  }
+  return m->ev_pool[m->ev_used++];
+}
+
+static cudaEvent_t stage_begin(Model* m) {
+  if (!m->timing) return nullptr;
+  cudaEvent_t e = next_event(m);
+  if (e) cudaEventRecord(e, m->c->stream);
+  return e;
+}
+
+static int32_t stage_end(Model* m, int cat, cudaEvent_t e0) {
+  if (!m->timing || !e0) return FLETCHER_OK;
+  cudaEvent_t e1 = next_event(m);
+  if (!e1) return set_error(m->c, FLETCHER_ERR_CUDA, "cudaEventCreate failed");
+  FL_CUDA(m->c, cudaEventRecord(e1, m->c->stream));
+  m->stage_recs.push_back({cat, e0, e1});
+  return FLETCHER_OK;
+}
+
 static int32_t forward_device(Model* m, const int32_t* d_ids, const int32_t* lengths, int32_t B, int32_t pooling,
                               float* d_out) {
   Ctx* c = m->c;
@@ -334,73 +369,80 @@ static int32_t forward_device(Model* m, const int32_t* d_ids, const int32_t* len
   int32_t n_tiles = 0, max_len = 0;
   if ((rc = upload_meta(m, lengths, B, T, &n_tiles, &max_len))) return rc;
   if ((rc = ensure_rope(m, max_len))) return rc;
-  if ((rc = launch_positions(c, m->d_cu, B, m->d_pos, max_len))) return rc;
   m->last_T = T;
-
   const int64_t H = m->H, I = m->I, Iup = m->Iup;
   const int32_t dt = m->dtype;
   const float eps = m->cfg.layer_norm_eps;
   const bool rope = m->cfg.position_type == 1;
-  if ((rc = launch_embed(c, dt, d_ids, m->d_pos, m->word, rope ? nullptr : m->ptab, m->cfg.max_positions, m->type0,
-                         m->eln_g, m->eln_b, m->X, T, H, eps)))
-    return rc;
+  // Each stage is optionally bracketed by CUDA events on the context's stream
+  // (Cuda_Model_SetStageTiming / Cuda_Model_StageTimes).
+#define FL_STAGE(cat, call)                  \
+  do {                                       \
+    cudaEvent_t e0_ = stage_begin(m);        \
+    if ((rc = (call))) return rc;            \
+    if ((rc = stage_end(m, (cat), e0_))) return rc; \
+  } while (0)
+  FL_STAGE(FLETCHER_STAGE_EMBED, launch_positions(c, m->d_cu, B, m->d_pos, max_len));
+  FL_STAGE(FLETCHER_STAGE_EMBED, launch_embed(c, dt, d_ids, m->d_pos, m->word, rope ? nullptr : m->ptab,
+                                              m->cfg.max_positions, m->type0, m->eln_g, m->eln_b, m->X, T, H, eps));
   const int64_t es = dtype_size(dt);
   const float scale = 1.0f / (float)std::sqrt((double)m->dh);
   const bool swiglu = m->cfg.activation == FLETCHER_ACT_SWIGLU;
   for (auto& L : m->layers) {
     if (dt == FLETCHER_F32) {
-      if ((rc = launch_sgemm(c, (float*)m->X, H, (float*)L.wqkv, 3 * H, (float*)m->QKV, 3 * H, T, 3 * H, H, L.bqkv,
-                             FLETCHER_ACT_IDENTITY)))
-        return rc;
-      if (rope && (rc = launch_rope_table(c, dt, m->QKV, T, 3 * H, 2 * H, (int32_t)m->dh, m->d_pos, m->cos_t, m->sin_t)))
-        return rc;
+      FL_STAGE(FLETCHER_STAGE_GEMM_QKV, launch_sgemm(c, (float*)m->X, H, (float*)L.wqkv, 3 * H, (float*)m->QKV, 3 * H, T,
+                                                     3 * H, H, L.bqkv, FLETCHER_ACT_IDENTITY));
+      if (rope)
+        FL_STAGE(FLETCHER_STAGE_ROPE, launch_rope_table(c, dt, m->QKV, T, 3 * H, 2 * H, (int32_t)m->dh, m->d_pos,
+                                                        m->cos_t, m->sin_t));
       float* qkv = (float*)m->QKV;
-      if ((rc = launch_attention_f32(c, qkv, qkv + H, qkv + 2 * H, 3 * H, (float*)m->CTX, H, m->d_cu, B, T,
-                                     (int32_t)m->nh, (int32_t)m->dh, scale, max_len)))
-        return rc;
-      if ((rc = launch_sgemm(c, (float*)m->CTX, H, (float*)L.wo, H, (float*)m->S, H, T, H, H, L.bo, FLETCHER_ACT_IDENTITY)))
-        return rc;
-      if ((rc = launch_add_layernorm(c, dt, m->X, m->S, m->X, L.ln1g, L.ln1b, T, H, eps))) return rc;
-      if ((rc = launch_sgemm(c, (float*)m->X, H, (float*)L.wi, Iup, (float*)m->INTER, Iup, T, Iup, H, L.bi,
-                             swiglu ? FLETCHER_ACT_IDENTITY : FLETCHER_ACT_GELU)))
-        return rc;
+      FL_STAGE(FLETCHER_STAGE_ATTENTION, launch_attention_f32(c, qkv, qkv + H, qkv + 2 * H, 3 * H, (float*)m->CTX, H,
+                                                              m->d_cu, B, T, (int32_t)m->nh, (int32_t)m->dh, scale,
+                                                              max_len));
+      FL_STAGE(FLETCHER_STAGE_GEMM_O, launch_sgemm(c, (float*)m->CTX, H, (float*)L.wo, H, (float*)m->S, H, T, H, H, L.bo,
+                                                   FLETCHER_ACT_IDENTITY));
+      FL_STAGE(FLETCHER_STAGE_LAYERNORM, launch_add_layernorm(c, dt, m->X, m->S, m->X, L.ln1g, L.ln1b, T, H, eps));
+      FL_STAGE(FLETCHER_STAGE_GEMM_UP, launch_sgemm(c, (float*)m->X, H, (float*)L.wi, Iup, (float*)m->INTER, Iup, T, Iup,
+                                                    H, L.bi, swiglu ? FLETCHER_ACT_IDENTITY : FLETCHER_ACT_GELU));
       const float* a_in = (float*)m->INTER;
       if (swiglu) {
-        if ((rc = launch_swiglu(c, dt, m->INTER, m->ACT, T, I))) return rc;
+        FL_STAGE(FLETCHER_STAGE_ACTIVATION, launch_swiglu(c, dt, m->INTER, m->ACT, T, I));
         a_in = (float*)m->ACT;
       }
-      if ((rc = launch_sgemm(c, a_in, I, (float*)L.wd, H, (float*)m->S, H, T, H, I, L.bd, FLETCHER_ACT_IDENTITY)))
-        return rc;
-      if ((rc = launch_add_layernorm(c, dt, m->X, m->S, m->X, L.ln2g, L.ln2b, T, H, eps))) return rc;
+      FL_STAGE(FLETCHER_STAGE_GEMM_DOWN, launch_sgemm(c, a_in, I, (float*)L.wd, H, (float*)m->S, H, T, H, I, L.bd,
+                                                      FLETCHER_ACT_IDENTITY));
+      FL_STAGE(FLETCHER_STAGE_LAYERNORM, launch_add_layernorm(c, dt, m->X, m->S, m->X, L.ln2g, L.ln2b, T, H, eps));
     } else {
       const bool fuse_rope = rope && m->dh == 64;
-      if ((rc = launch_gemm_tc(c, dt, fuse_rope ? EPI_ROPE : EPI_STORE, m->bn_qkv, m->X, T, H, L.wqkv, 3 * H, m->QKV,
-                               3 * H, L.bqkv, nullptr, 0, m->d_pos, m->cos_t, m->sin_t, rope ? 2 * H : 0)))
-        return rc;
-      if (rope && !fuse_rope &&
-          (rc = launch_rope_table(c, dt, m->QKV, T, 3 * H, 2 * H, (int32_t)m->dh, m->d_pos, m->cos_t, m->sin_t)))
-        return rc;
+      FL_STAGE(FLETCHER_STAGE_GEMM_QKV,
+               launch_gemm_tc(c, dt, fuse_rope ? EPI_ROPE : EPI_STORE, m->bn_qkv, m->X, T, H, L.wqkv, 3 * H, m->QKV,
+                              3 * H, L.bqkv, nullptr, 0, m->d_pos, m->cos_t, m->sin_t, rope ? 2 * H : 0));
+      if (rope && !fuse_rope)
+        FL_STAGE(FLETCHER_STAGE_ROPE, launch_rope_table(c, dt, m->QKV, T, 3 * H, 2 * H, (int32_t)m->dh, m->d_pos,
+                                                        m->cos_t, m->sin_t));
       const uint8_t* qkv = (const uint8_t*)m->QKV;
-      if ((rc = launch_flash_attention_ld(c, dt, qkv, qkv + H * es, qkv + 2 * H * es, 3 * H, m->CTX, H, m->d_cu,
-                                          m->d_tiles, n_tiles, (int32_t)m->nh, scale)))
-        return rc;
-      if ((rc = launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_o, m->CTX, T, H, L.wo, H, m->S, H, L.bo, m->X, H, nullptr,
-                               nullptr, nullptr, 0)))
-        return rc;
-      if ((rc = launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln1g, L.ln1b, T, H, eps))) return rc;
-      if ((rc = launch_gemm_tc(c, dt, swiglu ? EPI_SWIGLU : EPI_GELU, m->bn_up, m->X, T, H, L.wi, Iup, m->ACT, I, L.bi,
-                               nullptr, 0, nullptr, nullptr, nullptr, 0)))
-        return rc;
-      if ((rc = launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_d, m->ACT, T, I, L.wd, H, m->S, H, L.bd, m->X, H, nullptr,
-                               nullptr, nullptr, 0)))
-        return rc;
-      if ((rc = launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln2g, L.ln2b, T, H, eps))) return rc;
+      FL_STAGE(FLETCHER_STAGE_ATTENTION,
+               launch_flash_attention_ld(c, dt, qkv, qkv + H * es, qkv + 2 * H * es, 3 * H, m->CTX, H, m->d_cu,
+                                         m->d_tiles, n_tiles, (int32_t)m->nh, scale));
+      FL_STAGE(FLETCHER_STAGE_GEMM_O, launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_o, m->CTX, T, H, L.wo, H, m->S, H, L.bo,
+                                                     m->X, H, nullptr, nullptr, nullptr, 0));
+      FL_STAGE(FLETCHER_STAGE_LAYERNORM, launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln1g, L.ln1b, T, H, eps));
+      FL_STAGE(FLETCHER_STAGE_GEMM_UP, launch_gemm_tc(c, dt, swiglu ? EPI_SWIGLU : EPI_GELU, m->bn_up, m->X, T, H, L.wi,
+                                                      Iup, m->ACT, I, L.bi, nullptr, 0, nullptr, nullptr, nullptr, 0));
+      FL_STAGE(FLETCHER_STAGE_GEMM_DOWN, launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_d, m->ACT, T, I, L.wd, H, m->S, H,
+                                                        L.bd, m->X, H, nullptr, nullptr, nullptr, 0));
+      FL_STAGE(FLETCHER_STAGE_LAYERNORM, launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln2g, L.ln2b, T, H, eps));
     }
   }
-  if (pooling == FLETCHER_POOL_MEAN_L2) return launch_mean_pool_l2(c, dt, m->X, m->d_cu, B, H, d_out);
+  if (pooling == FLETCHER_POOL_MEAN_L2) {
+    FL_STAGE(FLETCHER_STAGE_POOL, launch_mean_pool_l2(c, dt, m->X, m->d_cu, B, H, d_out));
+    return FLETCHER_OK;
+  }
   // BertPooler.ForwardBatch (bert.go:441-488): CLS rows at cu_seqlens[i] -> fp32 Dense -> TanhFast.
-  if ((rc = launch_gather_rows_f32(c, dt, m->X, m->d_cu, B, H, m->d_cls))) return rc;
-  return launch_sgemm(c, m->d_cls, H, m->wp, H, d_out, H, B, H, H, m->bp, FLETCHER_ACT_TANH);
+  FL_STAGE(FLETCHER_STAGE_POOL, launch_gather_rows_f32(c, dt, m->X, m->d_cu, B, H, m->d_cls));
+  FL_STAGE(FLETCHER_STAGE_POOL, launch_sgemm(c, m->d_cls, H, m->wp, H, d_out, H, B, H, H, m->bp, FLETCHER_ACT_TANH));
+#undef FL_STAGE
+  return FLETCHER_OK;
 }
 
 static int32_t create(Ctx* c, const FletcherBertConfig* cfg, int32_t dtype, Model** out) {
@@ -449,6 +491,7 @@ static void destroy(Model* m) {
   cudaStreamSynchronize(c->stream);
   if (m->h_meta) cudaFreeHost(m->h_meta);
   if (m->meta_done) cudaEventDestroy(m->meta_done);
+  for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
   delete m;
 }
 
@@ -523,6 +566,38 @@ int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count
   dev_free(c, tmp, count * 4);
   FL_CUDA(c, cudaStreamSynchronize(c->stream));
   return rc;
+}
+
+int32_t Cuda_Model_SetStageTiming(CudaModelRef model, int32_t enable) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(m->c);
+  FL_CUDA(m->c, cudaStreamSynchronize(m->c->stream));
+  m->timing = enable != 0;
+  m->stage_recs.clear();
+  m->ev_used = 0;
+  return FLETCHER_OK;
+}
+
+int32_t Cuda_Model_StageTimes(CudaModelRef model, float* ms, int64_t* launches, int32_t n) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m || !ms || n <= 0) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(m->c);
+  FL_CUDA(m->c, cudaStreamSynchronize(m->c->stream));
+  for (int i = 0; i < n; i++) {
+    ms[i] = 0.f;
+    if (launches) launches[i] = 0;
+  }
+  for (auto& r : m->stage_recs) {
+    if (r.cat >= n) continue;
+    float t = 0.f;
+    FL_CUDA(m->c, cudaEventElapsedTime(&t, r.a, r.b));
+    ms[r.cat] += t;
+    if (launches) launches[r.cat]++;
+  }
+  m->stage_recs.clear();
+  m->ev_used = 0;
+  return FLETCHER_OK;
 }
 
 int32_t Cuda_Model_Free(CudaModelRef model) {

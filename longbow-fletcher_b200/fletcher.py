@@ -82,6 +82,9 @@ def _sig(L):
         "Cuda_Model_ForwardBatch": (i32, [vp, i32p, i32p, i32, i32, f32p]),
         "Cuda_Model_ForwardBatchDevice": (i32, [vp, vp, i32p, i32, i32, vp]),
         "Cuda_Model_LastHidden": (i32, [vp, f32p, i64]),
+        "Cuda_Model_SetStageTiming": (i32, [vp, i32]),
+        "Cuda_Model_StageTimes": (i32, [vp, f32p, i64p, i32]),
+        "Cuda_GetLaunchCount": (i64, [vp]),
         "Cuda_Model_Free": (i32, [vp]),
     }
     for name, (res, args) in sigs.items():
@@ -151,6 +154,9 @@ class Backend:
 
     def stream(self):
         return lib().Cuda_GetStream(self.ctx)
+
+    def launch_count(self):
+        return lib().Cuda_GetLaunchCount(self.ctx)
 
     def close(self):
         if self.ctx:
@@ -304,6 +310,20 @@ class BertModel:
         lens = np.ascontiguousarray(lengths, np.int32)
         self.be.check(lib().Cuda_Model_ForwardBatchDevice(self.h, ctypes.c_void_p(d_ids_ptr), _i32p(lens), lens.size,
                                                           pooling, ctypes.c_void_p(d_out_ptr)))
+
+    STAGES = ["embed", "gemm_qkv", "rope", "attention", "gemm_o", "layernorm", "gemm_up", "activation",
+              "gemm_down", "pool"]
+
+    def set_stage_timing(self, on: bool):
+        self.be.check(lib().Cuda_Model_SetStageTiming(self.h, int(on)))
+
+    def stage_times(self):
+        """{stage: (milliseconds, timed calls)} since the last read."""
+        n = len(self.STAGES)
+        ms = np.zeros(n, np.float32)
+        cnt = np.zeros(n, np.int64)
+        self.be.check(lib().Cuda_Model_StageTimes(self.h, _f32p(ms), cnt.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), n))
+        return {s: (float(ms[i]), int(cnt[i])) for i, s in enumerate(self.STAGES)}
 
     def last_hidden(self, T):
         out = np.empty((T, self.cfg.hidden), np.float32)
