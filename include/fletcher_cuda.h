@@ -169,6 +169,20 @@ int32_t Cuda_Attention_Fused(CudaContextRef ctx, CudaBufferRef q, CudaBufferRef 
 int32_t Cuda_Attention_VarLen(CudaContextRef ctx, CudaBufferRef q, CudaBufferRef k,
                               CudaBufferRef v, CudaBufferRef result, const int32_t* lengths,
                               int32_t numSeqs, int64_t hidden, int32_t numHeads, float scale);
+/* No counterpart in the reference.  Cuda_Attention_VarLen for callers that must not allocate
+ * device memory during the call (memory fully reserved by admission control, or an allocator
+ * owned by a host framework): the per-call metadata lives in one fixed device array per GPU
+ * of FLETCHER_NOALLOC_SCRATCH_INTS int32 (1 MiB, held until the process exits) instead of a
+ * per-call allocation.  A call needs numSeqs+1 ints (f32) or about numSeqs+1 + 2 per 64-row
+ * query tile (16-bit); larger batches return FLETCHER_ERR_INVALID.  All calls on a device
+ * share the array: calls that overlap on the GPU (two contexts or streams) race; calls on one
+ * context are ordered.  The first call on each device resolves the array's address
+ * (cudaGetSymbolAddress); make it before any stream capture. */
+#define FLETCHER_NOALLOC_SCRATCH_INTS (1 << 18)
+int32_t Cuda_Attention_VarLen_NoAlloc(CudaContextRef ctx, CudaBufferRef q, CudaBufferRef k,
+                                      CudaBufferRef v, CudaBufferRef result,
+                                      const int32_t* lengths, int32_t numSeqs, int64_t hidden,
+                                      int32_t numHeads, float scale);
 /* cuda_bridge.h:51-52 (cpu_backend.go:760-805): rotate-half RoPE in place, base 10000,
  * position = row % seqLen. */
 int32_t Cuda_ApplyRoPE(CudaContextRef ctx, CudaBufferRef data, int64_t batchSize, int64_t seqLen,

@@ -20,7 +20,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-DFLETCHER_BUILD"]
-SOURCES = ["context.cu", "ops.cu", "gemm_simt.cu", "gemm_tc.cu", "attention.cu", "model.cu", "abi_ops.cu"]
+SOURCES = ["context.cu", "ops.cu", "gemm_simt.cu", "gemm_tc.cu", "attention.cu", "model.cu", "abi_ops.cu",
+           "noalloc.cu"]
 
 
 def _deps():

@@ -73,6 +73,7 @@ def _sig(L):
         "Cuda_HasNaN": (i32, [vp, vp, i64, i32p]),
         "Cuda_Attention_Fused": (i32, [vp, vp, vp, vp, vp, i64, i64, i64, i32, f32]),
         "Cuda_Attention_VarLen": (i32, [vp, vp, vp, vp, vp, i32p, i32, i64, i32, f32]),
+        "Cuda_Attention_VarLen_NoAlloc": (i32, [vp, vp, vp, vp, vp, i32p, i32, i64, i32, f32]),
         "Cuda_ApplyRoPE": (i32, [vp, vp, i64, i64, i32, i32]),
         "Cuda_ApplyRoPE_VarLen": (i32, [vp, vp, i32p, i32, i32, i32, f32]),
         "Cuda_MeanPoolL2": (i32, [vp, vp, i32p, i32, i64, vp]),
