@@ -61,7 +61,7 @@ int32_t Cuda_Linear_Fused(CudaContextRef ctx, CudaBufferRef input, int64_t rows,
   int32_t rc;
   // 16-bit: tensor-core GEMM.  The (in,out) weight is packed K-major into a temporary (SwiGLU
   // weights gate/up-interleaved per tile) and the bias widened to fp32.
-  const int bn = (outCols % 256 == 0 && outCols >= 1024) ? 256 : 128;
+  const int bn = swiglu || (outCols % 256 == 0 && outCols >= 1024) ? 256 : 128;
   const bool tc_act = activation == FLETCHER_ACT_IDENTITY || activation == FLETCHER_ACT_GELU || swiglu;
   if (dt != FLETCHER_F32 && tc_act && gemm_tc_supported(rows, outCols, inCols, bn) && (!swiglu || outCols % bn == 0)) {
     Temp wk(c), bf(c);

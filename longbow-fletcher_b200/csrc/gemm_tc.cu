@@ -8,12 +8,15 @@
 // K-major [N, K] at model load (the reference stores Linear weights (in, out) = [K, N]).
 // Both are fetched by TMA in 128-byte-swizzled 64-wide K slabs.
 //
-// Kernel structure (persistent, one CTA per SM, 192 threads):
-//   warp 0  : TMA producer — one thread streams A/W slabs into a STAGES-deep smem ring;
-//   warp 1  : MMA issuer — one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two
-//             TMEM accumulators and commits to mbarriers; the warp also owns TMEM alloc;
-//   warps 2-5: epilogue — tcgen05.ld the accumulator (each warp reads its 32-lane quarter),
-//             apply bias / RoPE / GELU / SwiGLU / residual in registers, store 16-bit rows.
+// Kernel structure (persistent, one CTA per SM, 320 threads):
+//   warp 0   : TMA producer — one thread streams A/W slabs into a STAGES-deep smem ring;
+//   warp 1   : MMA issuer — one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two
+//              TMEM accumulators and commits to mbarriers; the warp also owns TMEM alloc;
+//   warps 2-9: epilogue — warp w reads TMEM lane quarter w%4 with tcgen05.ld (warps 2-5 take
+//              the first half of the tile's columns, warps 6-9 the second half), applies bias /
+//              RoPE / GELU / SwiGLU / residual in registers, writes 32x64 output boxes into a
+//              per-warp 128B-swizzled smem buffer and stores them with TMA bulk-tensor stores
+//              (full-line, asynchronous writes instead of per-thread 16-byte row stores).
 // Two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
 // Every mbarrier wait is bounded: on expiry the kernel records an error in a device flag,
 // raises a CTA-wide abort flag and all roles leave their loops.
@@ -29,6 +32,10 @@ namespace fl {
 namespace tc {
 
 constexpr int BM = 128, BK = 64;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;            // + producer warp + MMA warp
+constexpr int kStageOut = 32 * 128;                    // per-warp output box: 32 rows x 64 cols x 2 B
 constexpr long long kWaitLimitCycles = 4000000000LL;  // ~2 s at 2 GHz
 
 template <int BN>
@@ -37,8 +44,11 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int OUT_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = OUT_OFF + kEpiWarps * kStageOut;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = BAR_OFF + 256 /*barriers*/ + 1024 /*alignment slack*/;
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -87,6 +97,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Shared-memory matrix descriptor (tcgen05): K-major, 128-byte swizzle, 8-row groups 1024 B
 // apart (SBO), version 1, base offset 0.  The tile base must be 1024-byte aligned.
@@ -137,22 +156,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 }
 
 template <typename T>
-__device__ __forceinline__ void store32(T* dst, const float (&v)[32]) {
-  // 32 16-bit values = 64 bytes = 4 x 16-byte stores.
-  uint32_t w[16];
-#pragma unroll
-  for (int i = 0; i < 16; i++) {
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-      w[i] = *reinterpret_cast<uint32_t*>(&h);
-    } else {
-      __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-      w[i] = *reinterpret_cast<uint32_t*>(&h);
-    }
+__device__ __forceinline__ uint32_t pack2(float x, float y) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(x, y);
+    return *reinterpret_cast<uint32_t*>(&h);
   }
-  uint4* d = reinterpret_cast<uint4*>(dst);
+}
+
+// Writes this lane's row (64 values: a = columns 0-31, b = 32-63) of a 32x64 output box into
+// the warp's staging buffer in the TMA 128-byte swizzle layout: 16-byte chunk j of row r sits
+// at r*128 + (j ^ (r & 7))*16.
+template <typename T>
+__device__ __forceinline__ void stage_row(uint8_t* buf, int r, const float (&a)[32], const float (&b)[32]) {
+  uint8_t* row = buf + r * 128;
 #pragma unroll
-  for (int i = 0; i < 4; i++) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  for (int j = 0; j < 8; j++) {
+    const float* v = j < 4 ? &a[j * 8] : &b[(j - 4) * 8];
+    uint4 w = make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
+    *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) = w;
+  }
 }
 
 template <typename T>
@@ -165,13 +190,11 @@ __device__ __forceinline__ void load32(const T* src, float (&v)[32]) {
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
-        float2 f = __bfloat1622float2(h);
+        float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
         v[8 * i + 2 * j] = f.x;
         v[8 * i + 2 * j + 1] = f.y;
       } else {
-        __half2 h = *reinterpret_cast<const __half2*>(&w[j]);
-        float2 f = __half22float2(h);
+        float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
         v[8 * i + 2 * j] = f.x;
         v[8 * i + 2 * j + 1] = f.y;
       }
@@ -180,15 +203,16 @@ __device__ __forceinline__ void load32(const T* src, float (&v)[32]) {
 }
 
 template <typename T, int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* full = bars;
   uint64_t* empty = bars + C::STAGES;
   uint64_t* tfull = bars + 2 * C::STAGES;
@@ -208,7 +232,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], kEpiThreads);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -216,6 +240,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmC) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -282,8 +307,13 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5; warp w may read TMEM lanes [32*(w%4), 32*(w%4)+32).
+    // Epilogue.  Warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32): rows q*32.. of the tile.
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns
+    uint8_t* stg = smem + C::OUT_OFF + (warp - 2) * kStageOut;
+    // 64-column output units per warp: SwiGLU halves the width (BN/2 outputs per tile).
+    constexpr int UNITS = EPI == EPI_SWIGLU ? BN / 256 : BN / 128;
+    const int64_t n_out = EPI == EPI_SWIGLU ? args.N / 2 : args.N;
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int mb = tile / n_tiles, nb = tile % n_tiles;
@@ -291,90 +321,114 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort, args.err)) break;
       tc_fence_after();
-      const int64_t row = (int64_t)mb * BM + q * 32 + lane;
+      const int row0 = mb * BM + q * 32;
+      const int64_t row = (int64_t)row0 + lane;
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      T* out = reinterpret_cast<T*>(args.out);
-      if constexpr (EPI == EPI_SWIGLU) {
-        // Tile columns [0, BN/2) hold gate rows, [BN/2, BN) the matching up rows.
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; c++) {
-          float g[32], u[32];
-          tmem_ld32(tbase + c * 32, g);
-          tmem_ld32(tbase + BN / 2 + c * 32, u);
-          const int pcol = nb * BN + c * 32;  // packed column of the gate chunk
-          const int64_t ocol = (int64_t)nb * (BN / 2) + c * 32;
-          if (row_ok && ocol < args.N / 2) {
-            if (args.bias) {
+      for (int u = 0; u < UNITS; u++) {
+        float a[32], b[32];
+        int64_t ocol;
+        if constexpr (EPI == EPI_SWIGLU) {
+          // Tile columns [0, BN/2) hold gate rows, [BN/2, BN) the matching up rows; this unit
+          // produces output columns [half*64, half*64+64) of the tile's BN/2.
+          const int g0 = half * 64 + u * 64;  // gate column within the tile
+          float g[32], v[32];
+          tmem_ld32(tbase + g0, g);
+          tmem_ld32(tbase + BN / 2 + g0, v);
+          const int pcol = nb * BN + g0;
+          if (args.bias) {
 #pragma unroll
-              for (int i = 0; i < 32; i++) {
-                g[i] += args.bias[pcol + i];
-                u[i] += args.bias[pcol + BN / 2 + i];
-              }
+            for (int i = 0; i < 32; i++) {
+              g[i] += args.bias[pcol + i];
+              v[i] += args.bias[pcol + BN / 2 + i];
             }
-#pragma unroll
-            for (int i = 0; i < 32; i++) g[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * u[i];
-            store32<T>(out + row * args.ld_out + ocol, g);
           }
-        }
-      } else if constexpr (EPI == EPI_ROPE) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 64; c++) {
-          float x1[32], x2[32];
-          tmem_ld32(tbase + c * 64, x1);
-          tmem_ld32(tbase + c * 64 + 32, x2);
-          const int64_t col = (int64_t)nb * BN + c * 64;
-          if (row_ok && col < args.N) {
-            if (args.bias) {
 #pragma unroll
-              for (int i = 0; i < 32; i++) {
-                x1[i] += args.bias[col + i];
-                x2[i] += args.bias[col + 32 + i];
-              }
-            }
-            if (col < args.rope_cols) {
-              const int p = args.pos[row];
-              const float* ct = args.cos_t + (int64_t)p * 32;
-              const float* st = args.sin_t + (int64_t)p * 32;
+          for (int i = 0; i < 32; i++) a[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * v[i];
+          tmem_ld32(tbase + g0 + 32, g);
+          tmem_ld32(tbase + BN / 2 + g0 + 32, v);
+          if (args.bias) {
 #pragma unroll
-              for (int i = 0; i < 32; i++) {
-                const float a = x1[i], b = x2[i], cs = ct[i], sn = st[i];
-                x1[i] = a * cs - b * sn;
-                x2[i] = a * sn + b * cs;
-              }
+            for (int i = 0; i < 32; i++) {
+              g[i] += args.bias[pcol + 32 + i];
+              v[i] += args.bias[pcol + BN / 2 + 32 + i];
             }
-            store32<T>(out + row * args.ld_out + col, x1);
-            store32<T>(out + row * args.ld_out + col + 32, x2);
           }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c++) {
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
-          const int64_t col = (int64_t)nb * BN + c * 32;
-          if (row_ok && col < args.N) {
+#pragma unroll
+          for (int i = 0; i < 32; i++) b[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * v[i];
+          ocol = (int64_t)nb * (BN / 2) + g0;
+        } else {
+          const int c0 = half * (BN / 2) + u * 64;  // first column of the unit within the tile
+          tmem_ld32(tbase + c0, a);
+          tmem_ld32(tbase + c0 + 32, b);
+          ocol = (int64_t)nb * BN + c0;
+          if (ocol < args.N) {
             if (args.bias) {
 #pragma unroll
-              for (int i = 0; i < 32; i++) v[i] += args.bias[col + i];
+              for (int i = 0; i < 32; i++) {
+                a[i] += args.bias[ocol + i];
+                b[i] += args.bias[ocol + 32 + i];
+              }
+            }
+            if constexpr (EPI == EPI_ROPE) {
+              // Rotate-half on a 64-wide head: (x1, x2) = (a, b).
+              if (ocol < args.rope_cols && row_ok) {
+                const int p = args.pos[row];
+                const float4* ct = reinterpret_cast<const float4*>(args.cos_t + (int64_t)p * 32);
+                const float4* st = reinterpret_cast<const float4*>(args.sin_t + (int64_t)p * 32);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                  const float4 cv = __ldg(ct + i), sv = __ldg(st + i);
+                  const float cs[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                  for (int j = 0; j < 4; j++) {
+                    const float x1 = a[4 * i + j], x2 = b[4 * i + j];
+                    a[4 * i + j] = x1 * cs[j] - x2 * sn[j];
+                    b[4 * i + j] = x1 * sn[j] + x2 * cs[j];
+                  }
+                }
+              }
             }
             if constexpr (EPI == EPI_GELU) {
 #pragma unroll
-              for (int i = 0; i < 32; i++) v[i] = gelu_fast(v[i]);
+              for (int i = 0; i < 32; i++) {
+                a[i] = gelu_fast(a[i]);
+                b[i] = gelu_fast(b[i]);
+              }
             }
             if constexpr (EPI == EPI_RESIDUAL) {
-              float r[32];
-              load32<T>(reinterpret_cast<const T*>(args.residual) + row * args.ld_res + col, r);
+              if (row_ok) {
+                float r[32];
+                const T* rp = reinterpret_cast<const T*>(args.residual) + row * args.ld_res + ocol;
+                load32<T>(rp, r);
 #pragma unroll
-              for (int i = 0; i < 32; i++) v[i] += r[i];
+                for (int i = 0; i < 32; i++) a[i] += r[i];
+                load32<T>(rp + 32, r);
+#pragma unroll
+                for (int i = 0; i < 32; i++) b[i] += r[i];
+              }
             }
-            store32<T>(out + row * args.ld_out + col, v);
+          }
+        }
+        if (u == UNITS - 1) {  // every TMEM read of this tile is done: release the accumulator
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
+        if (ocol < n_out && row0 < args.M) {
+          if (lane == 0) bulk_wait_read0();  // the previous box has left the staging buffer
+          __syncwarp();
+          stage_row<T>(stg, lane, a, b);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, stg, (int)ocol, row0);  // rows >= M are clipped by TMA
+            bulk_commit();
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait0();
   }
 
   tc_fence_before();
@@ -400,14 +454,15 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2D K-major map: dims {K, rows}, box {64, box_rows}, 128-byte swizzle, OOB reads as zero.
-static int32_t make_map(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, uint64_t rows, uint64_t K,
-                        uint32_t box_rows) {
+// 2D row-major map over [rows, cols] with row stride ld (elements): box {box_cols, box_rows},
+// 128-byte swizzle, out-of-bounds reads as zero (stores are clipped).
+static int32_t make_map(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, uint64_t rows, uint64_t cols,
+                        uint64_t ld, uint32_t box_cols, uint32_t box_rows) {
   auto fn = encode_fn();
   if (!fn) return set_error(c, FLETCHER_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {K, rows};
-  cuuint64_t strides[1] = {K * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, dtype == FLETCHER_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -417,7 +472,7 @@ static int32_t make_map(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, 
 }
 
 template <typename T, int BN, int EPI>
-static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, GemmArgs a) {
+static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmArgs a) {
   using Cf = Cfg<BN>;
   static bool attr_set[64] = {};  // per device
   if (!attr_set[c->device & 63]) {
@@ -428,22 +483,24 @@ static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, GemmArg
   a.num_n_tiles = (int)((a.N + BN - 1) / BN);
   const int tiles = a.num_m_tiles * a.num_n_tiles;
   const int grid = tiles < c->num_sms ? tiles : c->num_sms;
-  k_gemm_tc<T, BN, EPI><<<grid, 192, Cf::SMEM, c->stream>>>(ma, mb, a);
+  k_gemm_tc<T, BN, EPI><<<grid, kThreads, Cf::SMEM, c->stream>>>(ma, mb, mc, a);
   FL_LAUNCH(c);
   return FLETCHER_OK;
 }
 
 template <typename T>
-static int32_t dispatch(Ctx* c, int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a) {
-#define FL_EPI(E)                                                      \
-  case E:                                                              \
-    return bn == 256 ? run<T, 256, E>(c, ma, mb, a) : run<T, 128, E>(c, ma, mb, a);
+static int32_t dispatch(Ctx* c, int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                        const GemmArgs& a) {
+#define FL_EPI(E)                                                                \
+  case E:                                                                        \
+    return bn == 256 ? run<T, 256, E>(c, ma, mb, mc, a) : run<T, 128, E>(c, ma, mb, mc, a);
   switch (epi) {
     FL_EPI(EPI_STORE)
     FL_EPI(EPI_ROPE)
     FL_EPI(EPI_GELU)
-    FL_EPI(EPI_SWIGLU)
     FL_EPI(EPI_RESIDUAL)
+    case EPI_SWIGLU:
+      return run<T, 256, EPI_SWIGLU>(c, ma, mb, mc, a);
   }
 #undef FL_EPI
   return set_error(c, FLETCHER_ERR_INVALID, "gemm: unknown epilogue %d", epi);
@@ -452,7 +509,7 @@ static int32_t dispatch(Ctx* c, int epi, int bn, const CUtensorMap& ma, const CU
 }  // namespace tc
 
 bool gemm_tc_supported(int64_t M, int64_t N, int64_t K, int bn) {
-  return M > 0 && K % tc::BK == 0 && K > 0 && N % 64 == 0 && (bn == 128 || bn == 256);
+  return M > 0 && M < (1ll << 31) && K % tc::BK == 0 && K > 0 && N % 64 == 0 && (bn == 128 || bn == 256);
 }
 
 int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, int64_t M, int64_t K, const void* W,
@@ -463,11 +520,16 @@ int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, in
            (long long)M, (long long)N, (long long)K, bn);
   FL_CHECK(c, ((uintptr_t)A & 15) == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)out & 15) == 0 && ld_out % 8 == 0,
            "gemm_tc: operands must be 16-byte aligned");
-  FL_CHECK(c, epi != EPI_SWIGLU || N % bn == 0, "gemm_tc: SwiGLU needs N %% BN == 0");
-  CUtensorMap ma, mb;
-  int32_t rc = tc::make_map(c, &ma, dtype, A, (uint64_t)M, (uint64_t)K, tc::BM);
+  FL_CHECK(c, epi != EPI_SWIGLU || (bn == 256 && N % 256 == 0), "gemm_tc: SwiGLU needs BN = 256 and N %% 256 == 0");
+  FL_CHECK(c, epi != EPI_RESIDUAL || (((uintptr_t)residual & 15) == 0 && ld_res % 8 == 0),
+           "gemm_tc: residual must be 16-byte aligned");
+  const int64_t n_out = epi == EPI_SWIGLU ? N / 2 : N;
+  CUtensorMap ma, mb, mc;
+  int32_t rc = tc::make_map(c, &ma, dtype, A, (uint64_t)M, (uint64_t)K, (uint64_t)K, tc::BK, tc::BM);
   if (rc) return rc;
-  rc = tc::make_map(c, &mb, dtype, W, (uint64_t)N, (uint64_t)K, (uint32_t)bn);
+  rc = tc::make_map(c, &mb, dtype, W, (uint64_t)N, (uint64_t)K, (uint64_t)K, tc::BK, (uint32_t)bn);
+  if (rc) return rc;
+  rc = tc::make_map(c, &mc, dtype, out, (uint64_t)M, (uint64_t)n_out, (uint64_t)ld_out, 64, 32);
   if (rc) return rc;
   GemmArgs a{};
   a.M = M;
@@ -483,8 +545,8 @@ int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, in
   a.sin_t = sin_t;
   a.rope_cols = rope_cols;
   a.err = c->d_err;
-  if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16>(c, epi, bn, ma, mb, a);
-  return tc::dispatch<__half>(c, epi, bn, ma, mb, a);
+  if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16>(c, epi, bn, ma, mb, mc, a);
+  return tc::dispatch<__half>(c, epi, bn, ma, mb, mc, a);
 }
 
 }  // namespace fl

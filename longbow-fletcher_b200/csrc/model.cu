@@ -468,10 +468,11 @@ static int32_t create(Ctx* c, const FletcherBertConfig* cfg, int32_t dtype, Mode
   m->nh = cfg->num_heads;
   m->dh = dh;
   // Tile widths: 256-wide tiles for the wide GEMMs, 128 where N is small.
+  // (SwiGLU needs 256 so that a tile holds 128 gate and 128 up columns.)
   m->bn_qkv = (3 * m->H) % 256 == 0 && 3 * m->H >= 1024 ? 256 : 128;
-  m->bn_o = 128;
-  m->bn_d = 128;
-  m->bn_up = m->Iup % 256 == 0 && m->Iup >= 1024 ? 256 : 128;
+  m->bn_o = m->H % 256 == 0 ? 256 : 128;
+  m->bn_d = m->bn_o;
+  m->bn_up = cfg->activation == FLETCHER_ACT_SWIGLU || (m->Iup % 256 == 0 && m->Iup >= 1024) ? 256 : 128;
   if (cudaEventCreateWithFlags(&m->meta_done, cudaEventDisableTiming) != cudaSuccess) {
     delete m;
     return set_error(c, FLETCHER_ERR_CUDA, "cudaEventCreate failed");
