@@ -173,7 +173,7 @@ int32_t Cuda_Attention_VarLen(CudaContextRef ctx, CudaBufferRef q, CudaBufferRef
  * device memory during the call (memory fully reserved by admission control, or an allocator
  * owned by a host framework): the per-call metadata lives in one fixed device array per GPU
  * of FLETCHER_NOALLOC_SCRATCH_INTS int32 (1 MiB, held until the process exits) instead of a
- * per-call allocation.  A call needs numSeqs+1 ints (f32) or about numSeqs+1 + 2 per 64-row
+ * per-call allocation.  A call needs numSeqs+1 ints (f32) or about numSeqs+1 + 2 per 128-row
  * query tile (16-bit); larger batches return FLETCHER_ERR_INVALID.  All calls on a device
  * share the array: calls that overlap on the GPU (two contexts or streams) race; calls on one
  * context are ordered.  The first call on each device resolves the array's address

@@ -262,11 +262,11 @@ static int32_t attention_common(Ctx* c, Buf* q, Buf* k, Buf* v, Buf* out, const 
   FL_CHECK(c, dh == 64, "Attention: 16-bit attention needs head_dim 64 (got %d)", dh);
   std::vector<int2> tiles;
   for (int s = 0; s < Bn; s++)
-    for (int q0 = 0; q0 < lens[s]; q0 += 64) tiles.push_back(make_int2(s, q0));
+    for (int q0 = 0; q0 < lens[s]; q0 += kAttnTileRows) tiles.push_back(make_int2(s, q0));
   Temp dt_(c);
   if ((rc = upload(c, dt_, tiles.data(), (int64_t)tiles.size() * 8))) return rc;
-  return launch_flash_attention_ld(c, dt, q->ptr, k->ptr, v->ptr, hidden, out->ptr, hidden, (const int32_t*)dcu.p,
-                                   (const int2*)dt_.p, (int32_t)tiles.size(), nh, scale);
+  return launch_flash_attention_tc(c, dt, q->ptr, k->ptr, v->ptr, hidden, T, hidden, out->ptr, hidden,
+                                   (const int32_t*)dcu.p, (const int2*)dt_.p, (int32_t)tiles.size(), nh, scale);
 }
 
 int32_t Cuda_Attention_Fused(CudaContextRef ctx, CudaBufferRef q, CudaBufferRef k, CudaBufferRef v,

@@ -59,6 +59,15 @@ int32_t launch_flash_attention_ld(Ctx* c, int32_t dtype, const void* q, const vo
                                   int64_t ld_in, void* out, int64_t ld_out, const int32_t* cu_seqlens,
                                   const int2* tiles, int32_t num_tiles, int32_t nh, float scale);
 
+// bf16/f16 flash attention on tcgen05 (attention_tc.cu), head_dim 64: q/k/v [T, H] views with
+// row stride ld_in; tiles128: int2 {seq, q_row_start} per 128-row query tile.
+int32_t launch_flash_attention_tc(Ctx* c, int32_t dtype, const void* q, const void* k, const void* v,
+                                  int64_t ld_in, int64_t T, int64_t H, void* out, int64_t ld_out,
+                                  const int32_t* cu_seqlens, const int2* tiles128, int32_t num_tiles,
+                                  int32_t nh, float scale);
+// Query-tile height of launch_flash_attention_tc.
+constexpr int kAttnTileRows = 128;
+
 // Elementwise helpers.
 int32_t launch_scale_add(Ctx* c, int32_t dtype, void* x, const void* other, float scale,
                          float add, int64_t n);  // x = x*scale + add (+ other)

@@ -290,7 +290,7 @@ static int32_t upload_meta(Model* m, const int32_t* lengths, int32_t B, int64_t 
   int64_t nt = 0;
   int32_t mx = 0;
   for (int i = 0; i < B; i++) {
-    nt += (lengths[i] + 63) / 64;
+    nt += (lengths[i] + kAttnTileRows - 1) / kAttnTileRows;
     mx = std::max(mx, lengths[i]);
   }
   FL_CHECK(c, nt <= m->tiles_cap, "internal: tile list overflow");
@@ -314,7 +314,7 @@ static int32_t upload_meta(Model* m, const int32_t* lengths, int32_t B, int64_t 
   int64_t k = 0;
   for (int oi = 0; oi < B; oi++) {
     const int s = order[oi];
-    for (int q0 = 0; q0 < lengths[s]; q0 += 64) tl[k++] = make_int2(s, q0);
+    for (int q0 = 0; q0 < lengths[s]; q0 += kAttnTileRows) tl[k++] = make_int2(s, q0);
   }
   FL_CUDA(c, cudaMemcpyAsync(m->d_cu, cu, (B + 1) * 4, cudaMemcpyHostToDevice, c->stream));
   if (nt) FL_CUDA(c, cudaMemcpyAsync(m->d_tiles, tl, nt * 8, cudaMemcpyHostToDevice, c->stream));
@@ -422,8 +422,8 @@ static int32_t forward_device(Model* m, const int32_t* d_ids, const int32_t* len
                                                         m->cos_t, m->sin_t));
       const uint8_t* qkv = (const uint8_t*)m->QKV;
       FL_STAGE(FLETCHER_STAGE_ATTENTION,
-               launch_flash_attention_ld(c, dt, qkv, qkv + H * es, qkv + 2 * H * es, 3 * H, m->CTX, H, m->d_cu,
-                                         m->d_tiles, n_tiles, (int32_t)m->nh, scale));
+               launch_flash_attention_tc(c, dt, qkv, qkv + H * es, qkv + 2 * H * es, 3 * H, T, H, m->CTX, H,
+                                         m->d_cu, m->d_tiles, n_tiles, (int32_t)m->nh, scale));
       FL_STAGE(FLETCHER_STAGE_GEMM_O, launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_o, m->CTX, T, H, L.wo, H, m->S, H, L.bo,
                                                      m->X, H, nullptr, nullptr, nullptr, 0));
       FL_STAGE(FLETCHER_STAGE_LAYERNORM, launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln1g, L.ln1b, T, H, eps));

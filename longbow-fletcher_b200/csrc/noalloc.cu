@@ -1,7 +1,7 @@
 // Cuda_Attention_VarLen_NoAlloc: variable-length attention that allocates no memory.
 //
 // Cuda_Attention_VarLen allocates a small device array per call for its launch metadata (the
-// cu_seqlens prefix sums and, in 16-bit mode, the list of 64-row query tiles).  Some callers
+// cu_seqlens prefix sums and, in 16-bit mode, the list of 128-row query tiles).  Some callers
 // cannot allocate at that point: a server whose device memory is fully reserved up front by
 // its admission control (every byte is accounted before a request is accepted), or a host
 // framework that owns the device allocator and forbids other allocations.  This entry point
@@ -11,8 +11,8 @@
 // Limits and sharing rules:
 //   - the array holds FLETCHER_NOALLOC_SCRATCH_INTS int32 values (1 MiB) on every GPU that
 //     loads the library, for the life of the process;
-//   - one call needs (numSeqs + 1) ints in 32-bit mode, plus 2 ints per 64-row query tile
-//     (sum over sequences of ceil(length / 64)) in 16-bit mode; larger calls are rejected with
+//   - one call needs (numSeqs + 1) ints in 32-bit mode, plus 2 ints per 128-row query tile
+//     (sum over sequences of ceil(length / 128)) in 16-bit mode; larger calls are rejected with
 //     FLETCHER_ERR_INVALID before anything is launched;
 //   - every call on a device shares the one array and it keeps the previous call's contents
 //     (each call rewrites the part it reads, so nothing has to start at zero); calls whose work
@@ -77,7 +77,7 @@ extern "C" int32_t Cuda_Attention_VarLen_NoAlloc(CudaContextRef ctx, CudaBufferR
   for (int i = 0; i < numSeqs; i++) {
     FL_CHECK(c, lengths[i] >= 0, "AttentionVarLen_NoAlloc: negative length");
     T += lengths[i];
-    tiles += (lengths[i] + 63) / 64;
+    tiles += (lengths[i] + kAttnTileRows - 1) / kAttnTileRows;
     mx = lengths[i] > mx ? lengths[i] : mx;
   }
   const int64_t es = dtype_size(dt);
@@ -100,7 +100,7 @@ extern "C" int32_t Cuda_Attention_VarLen_NoAlloc(CudaContextRef ctx, CudaBufferR
   if (dt != FLETCHER_F32) {
     int64_t t = tiles_off;
     for (int s = 0; s < numSeqs; s++)
-      for (int q0 = 0; q0 < lengths[s]; q0 += 64) {
+      for (int q0 = 0; q0 < lengths[s]; q0 += kAttnTileRows) {
         g_host[t++] = s;
         g_host[t++] = q0;
       }
@@ -109,6 +109,6 @@ extern "C" int32_t Cuda_Attention_VarLen_NoAlloc(CudaContextRef ctx, CudaBufferR
   if (dt == FLETCHER_F32)
     return launch_attention_f32(c, (const float*)q->ptr, (const float*)k->ptr, (const float*)v->ptr, hidden,
                                 (float*)o->ptr, hidden, dscr, numSeqs, T, nh, dh, scale, mx);
-  return launch_flash_attention_ld(c, dt, q->ptr, k->ptr, v->ptr, hidden, o->ptr, hidden, dscr,
+  return launch_flash_attention_tc(c, dt, q->ptr, k->ptr, v->ptr, hidden, T, hidden, o->ptr, hidden, dscr,
                                    reinterpret_cast<const int2*>(dscr + tiles_off), (int32_t)tiles, nh, scale);
 }
