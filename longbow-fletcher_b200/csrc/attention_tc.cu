@@ -60,6 +60,19 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed two-lane fp32 FMA / add (sm_100): one instruction for two values.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
+  asm("{\n .reg .b64 a, b, c, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n mov.b64 c, {%6, %7};\n"
+      " fma.rn.f32x2 d, a, b, c;\n mov.b64 {%0, %1}, d;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1) {
+  asm("{\n .reg .b64 a, d;\n mov.b64 d, {%0, %1};\n mov.b64 a, {%2, %3};\n add.rn.f32x2 d, d, a;\n"
+      " mov.b64 {%0, %1}, d;\n}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1));
+}
 
 __device__ __forceinline__ Work decode(const AttnArgs& a, int w) {
   const int2 t = a.tiles[w / a.nh];
@@ -272,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         m = mx;
         // Pass 2: P = exp2(S*scale*log2e - max) -> smem (row r, 64 keys = 128 B, 128-byte swizzle,
         // K-major for the PV MMA).  P buffer g&1 is free: PV_{g-2} finished before O_{g-2} was read.
-        float rs = 0.f;
+        float rs0 = 0.f, rs1 = 0.f;
         uint8_t* prow = smem + OFF_P + b * P_BYTES + r * 128;
 #pragma unroll
         for (int hf = 0; hf < 2; hf++) {
@@ -283,10 +296,14 @@ __global__ void __launch_bounds__(kThreads, 2)
             for (int i = 0; i < 32; i++) sv[i] = hf * 32 + i < valid ? ex2(fmaf(sv[i], sl2, -ms)) : 0.f;
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; i++) sv[i] = ex2(fmaf(sv[i], sl2, -ms));
+            for (int i = 0; i < 32; i += 2) {
+              fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
+              sv[i] = ex2(sv[i]);
+              sv[i + 1] = ex2(sv[i + 1]);
+            }
           }
 #pragma unroll
-          for (int i = 0; i < 32; i++) rs += sv[i];
+          for (int i = 0; i < 32; i += 2) add2(rs0, rs1, sv[i], sv[i + 1]);
 #pragma unroll
           for (int c = 0; c < 4; c++) {
             const float* v = &sv[c * 8];
@@ -296,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = wv;
           }
         }
-        l = l * corr + rs;
+        l = l * corr + (rs0 + rs1);
         fence_async_smem();
         tc_fence_before();
         mbar_arrive(&p_full[b]);
@@ -314,7 +331,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             float tt[32];
             tmem_ld32(tmem + lane_off + 2 * BKV + bo * D + hf * 32, tt);
 #pragma unroll
-            for (int c = 0; c < 32; c++) o[hf * 32 + c] = fmaf(o[hf * 32 + c], f, tt[c]);
+            for (int c = 0; c < 32; c += 2)
+            fma2(o[hf * 32 + c], o[hf * 32 + c + 1], o[hf * 32 + c], o[hf * 32 + c + 1], f, f, tt[c], tt[c + 1]);
           }
           tc_fence_before();
           mbar_arrive(&o_free[bo]);
@@ -339,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           float tt[32];
           tmem_ld32(tmem + lane_off + 2 * BKV + bo * D + hf * 32, tt);
 #pragma unroll
-          for (int c = 0; c < 32; c++) o[hf * 32 + c] = fmaf(o[hf * 32 + c], f, tt[c]);
+          for (int c = 0; c < 32; c += 2)
+            fma2(o[hf * 32 + c], o[hf * 32 + c + 1], o[hf * 32 + c], o[hf * 32 + c + 1], f, f, tt[c], tt[c + 1]);
         }
         store_row<T>(args, prev, r, o, l);
       }

@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
         const int mb = tile / n_tiles, nb = tile % n_tiles;
         for (int kb = 0; kb < num_kb; kb++) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort, args.err)) goto producer_done;
+          if (!mbar_wait_spin(&empty[stage], phase ^ 1, abort, args.err)) goto producer_done;
           mbar_expect_tx(&full[stage], C::STAGE_BYTES);
           tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, mb * BM);
           tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
@@ -167,12 +167,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort, args.err)) break;
+        if (!mbar_wait_spin(&tempty[acc], acc_phase ^ 1, abort, args.err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < num_kb; kb++) {
-          if (!mbar_wait(&full[stage], phase, abort, args.err)) {
+          if (!mbar_wait_spin(&full[stage], phase, abort, args.err)) {
             ok = false;
             break;
           }
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int mb = tile / n_tiles, nb = tile % n_tiles;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort, args.err)) break;
+      if (!mbar_wait_spin(&tfull[acc], acc_phase, abort, args.err)) break;
       tc_fence_after();
       const int row0 = mb * BM + q * 32;
       const int64_t row = (int64_t)row0 + lane;

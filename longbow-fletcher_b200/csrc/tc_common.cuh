@@ -43,7 +43,23 @@ __device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait.  Returns false when this CTA is aborting (timeout here or elsewhere).
+// Bounded spin wait (latency first; for kernels whose waiting threads do not compete with
+// compute warps for issue slots).  Returns false when this CTA is aborting.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort, int32_t* err) {
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 0) {
+      if (*abort) return false;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        atomicExch(err, kDevWaitTimeout);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+// Bounded sleeping wait.  Returns false when this CTA is aborting (timeout here or elsewhere).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int32_t* err) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
