@@ -264,60 +264,42 @@ __global__ void __launch_bounds__(kThreads, 2)
           m = -INFINITY;
           l = 0.f;
         }
-        // Pass 1: row max over the block (S stays in TMEM; two 32-column loads).
-        const bool partial = valid < BKV;  // only a sequence's last block needs the key mask
+        // The block's S row (one 64-column TMEM load), masked past the sequence end.
+        float sv[BKV];
+        tmem_ld64(tmem + lane_off + b * BKV, sv);
+        tc_fence_before();
+        mbar_arrive(&s_free[b]);
+        if (valid < BKV) {  // only a sequence's last block needs the key mask
+#pragma unroll
+          for (int i = 0; i < BKV; i++)
+            if (i >= valid) sv[i] = -INFINITY;
+        }
         float mx = m;
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
-          float sv[32];
-          tmem_ld32(tmem + lane_off + b * BKV + hf * 32, sv);
-          if (partial) {
-#pragma unroll
-            for (int i = 0; i < 32; i++)
-              if (hf * 32 + i < valid) mx = fmaxf(mx, sv[i]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; i++) mx = fmaxf(mx, sv[i]);
-          }
-        }
+        for (int i = 0; i < BKV; i++) mx = fmaxf(mx, sv[i]);
         const float corr = ex2((m - mx) * sl2);
         const float ms = mx * sl2;
         m = mx;
-        // Pass 2: P = exp2(S*scale*log2e - max) -> smem (row r, 64 keys = 128 B, 128-byte swizzle,
-        // K-major for the PV MMA).  P buffer g&1 is free: PV_{g-2} finished before O_{g-2} was read.
+        // P = exp2(S*scale*log2e - max) -> smem (row r, 64 keys = 128 B, 128-byte swizzle, K-major
+        // for the PV MMA).  P buffer g&1 is free: PV_{g-2} finished before O_{g-2} was read.
         float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < BKV; i += 2) {
+          fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
+          sv[i] = ex2(sv[i]);
+          sv[i + 1] = ex2(sv[i + 1]);
+          add2(rs0, rs1, sv[i], sv[i + 1]);
+        }
         uint8_t* prow = smem + OFF_P + b * P_BYTES + r * 128;
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
-          float sv[32];
-          tmem_ld32(tmem + lane_off + b * BKV + hf * 32, sv);
-          if (partial) {
-#pragma unroll
-            for (int i = 0; i < 32; i++) sv[i] = hf * 32 + i < valid ? ex2(fmaf(sv[i], sl2, -ms)) : 0.f;
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
-              sv[i] = ex2(sv[i]);
-              sv[i + 1] = ex2(sv[i + 1]);
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) add2(rs0, rs1, sv[i], sv[i + 1]);
-#pragma unroll
-          for (int c = 0; c < 4; c++) {
-            const float* v = &sv[c * 8];
-            const int ch = hf * 4 + c;
-            uint4 wv =
-                make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
-            *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = wv;
-          }
+        for (int c = 0; c < 8; c++) {
+          const float* v = &sv[c * 8];
+          uint4 wv = make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = wv;
         }
         l = l * corr + (rs0 + rs1);
         fence_async_smem();
-        tc_fence_before();
         mbar_arrive(&p_full[b]);
-        mbar_arrive(&s_free[b]);
         if (g >= 1) {  // O_{g-1} is ready once PV_{g-1} ran; that also frees P buffer (g-1)&1
           const int i = g - 1, bo = i & 1;
           if (!mbar_wait(&o_full[bo], (i >> 1) & 1, abort, args.err)) {
@@ -326,13 +308,11 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
           tc_fence_after();
           const float f = exp2f((m_o - m_pb) * sl2);
+          {
+            float tt[D];
+            tmem_ld64(tmem + lane_off + 2 * BKV + bo * D, tt);
 #pragma unroll
-          for (int hf = 0; hf < 2; hf++) {
-            float tt[32];
-            tmem_ld32(tmem + lane_off + 2 * BKV + bo * D + hf * 32, tt);
-#pragma unroll
-            for (int c = 0; c < 32; c += 2)
-            fma2(o[hf * 32 + c], o[hf * 32 + c + 1], o[hf * 32 + c], o[hf * 32 + c + 1], f, f, tt[c], tt[c + 1]);
+            for (int c = 0; c < D; c += 2) fma2(o[c], o[c + 1], o[c], o[c + 1], f, f, tt[c], tt[c + 1]);
           }
           tc_fence_before();
           mbar_arrive(&o_free[bo]);
@@ -352,13 +332,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (mbar_wait(&o_full[bo], (i >> 1) & 1, abort, args.err)) {
         tc_fence_after();
         const float f = exp2f((m_o - m) * sl2);
+        {
+          float tt[D];
+          tmem_ld64(tmem + lane_off + 2 * BKV + bo * D, tt);
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
-          float tt[32];
-          tmem_ld32(tmem + lane_off + 2 * BKV + bo * D + hf * 32, tt);
-#pragma unroll
-          for (int c = 0; c < 32; c += 2)
-            fma2(o[hf * 32 + c], o[hf * 32 + c + 1], o[hf * 32 + c], o[hf * 32 + c + 1], f, f, tt[c], tt[c + 1]);
+          for (int c = 0; c < D; c += 2) fma2(o[c], o[c + 1], o[c], o[c + 1], f, f, tt[c], tt[c + 1]);
         }
         store_row<T>(args, prev, r, o, l);
       }
