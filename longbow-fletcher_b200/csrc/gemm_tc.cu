@@ -211,6 +211,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = (int64_t)row0 + lane;
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      // RoPE: every 64-wide head of this row uses the same cos/sin (same position, same
+      // frequencies), so the row's table entries are loaded once per tile, not once per head.
+      float rc[EPI == EPI_ROPE ? 32 : 1], rs[EPI == EPI_ROPE ? 32 : 1];
+      if constexpr (EPI == EPI_ROPE) {
+        if (row_ok && (int64_t)nb * BN < args.rope_cols) {
+          const int p = args.pos[row];
+          const float4* ct = reinterpret_cast<const float4*>(args.cos_t + (int64_t)p * 32);
+          const float4* st = reinterpret_cast<const float4*>(args.sin_t + (int64_t)p * 32);
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const float4 cv = __ldg(ct + i), sv = __ldg(st + i);
+            rc[4 * i] = cv.x; rc[4 * i + 1] = cv.y; rc[4 * i + 2] = cv.z; rc[4 * i + 3] = cv.w;
+            rs[4 * i] = sv.x; rs[4 * i + 1] = sv.y; rs[4 * i + 2] = sv.z; rs[4 * i + 3] = sv.w;
+          }
+        }
+      }
 #pragma unroll 1
       for (int u = 0; u < UNITS; u++) {
         float a[32], b[32];
@@ -260,19 +276,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (EPI == EPI_ROPE) {
               // Rotate-half on a 64-wide head: (x1, x2) = (a, b).
               if (ocol < args.rope_cols && row_ok) {
-                const int p = args.pos[row];
-                const float4* ct = reinterpret_cast<const float4*>(args.cos_t + (int64_t)p * 32);
-                const float4* st = reinterpret_cast<const float4*>(args.sin_t + (int64_t)p * 32);
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                  const float4 cv = __ldg(ct + i), sv = __ldg(st + i);
-                  const float cs[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-                  for (int j = 0; j < 4; j++) {
-                    const float x1 = a[4 * i + j], x2 = b[4 * i + j];
-                    a[4 * i + j] = x1 * cs[j] - x2 * sn[j];
-                    b[4 * i + j] = x1 * sn[j] + x2 * cs[j];
-                  }
+                for (int i = 0; i < 32; i++) {
+                  const float x1 = a[i], x2 = b[i];
+                  a[i] = x1 * rc[i] - x2 * rs[i];
+                  b[i] = x1 * rs[i] + x2 * rc[i];
                 }
               }
             }
