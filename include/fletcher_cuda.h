@@ -214,6 +214,10 @@ int32_t Cuda_Model_ForwardBatch(CudaModelRef model, const int32_t* ids, const in
 int32_t Cuda_Model_ForwardBatchDevice(CudaModelRef model, const int32_t* d_ids,
                                       const int32_t* lengths, int32_t numSeqs, int32_t pooling,
                                       float* d_out);
+/* CUDA-graph replay of repeated batch shapes (on by default): a shape (lengths, pooling,
+ * buffers) runs eagerly the first time, is captured the second time and replayed after that,
+ * which removes per-kernel host launch cost.  Disabling also drops the cached graphs. */
+int32_t Cuda_Model_SetGraphs(CudaModelRef model, int32_t enable);
 /* Stage timing: when enabled, every stage of the forward pass is bracketed by CUDA events on
  * the context's stream.  Cuda_Model_StageTimes synchronises, writes the summed milliseconds
  * (and the number of timed calls) per stage since the last read into ms[n] / launches[n]

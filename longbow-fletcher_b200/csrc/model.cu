@@ -65,6 +65,17 @@ struct Model {
   uint8_t* h_meta = nullptr;
   int64_t h_meta_cap = 0;
   cudaEvent_t meta_done = nullptr;
+  // CUDA graphs of the kernel sequence, per batch shape
+  struct GraphEntry {
+    std::vector<int32_t> key;
+    cudaGraphExec_t exec;
+    uint64_t last_use;
+    int64_t kernels;
+  };
+  bool use_graphs = true;
+  std::vector<GraphEntry> graphs;
+  std::vector<std::vector<int32_t>> graph_seen;
+  uint64_t graph_tick = 0;
   int64_t last_T = 0;
   // stage timing
   bool timing = false;
@@ -83,7 +94,10 @@ static int32_t own(Model* m, void** p, int64_t bytes) {
   return rc;
 }
 
+void clear_graphs(Model* m);
+
 static void free_ws(Model* m) {
+  clear_graphs(m);  // captured graphs hold the old workspace pointers
   for (auto& a : m->ws) dev_free(m->c, a.first, a.second);
   m->ws.clear();
   m->ws_T = 0;
@@ -132,6 +146,7 @@ static int32_t ensure_rope(Model* m, int32_t need) {
   if ((rc = dev_alloc(m->c, (void**)&m->cos_t, (int64_t)len * (m->dh / 2) * 4))) return rc;
   if ((rc = dev_alloc(m->c, (void**)&m->sin_t, (int64_t)len * (m->dh / 2) * 4))) return rc;
   m->rope_len = len;
+  clear_graphs(m);  // captured graphs hold the old table pointers
   return launch_rope_build_table(m->c, m->cos_t, m->sin_t, len, (int32_t)m->dh, (double)m->cfg.rope_base);
 }
 
@@ -351,6 +366,9 @@ static int32_t stage_end(Model* m, int cat, cudaEvent_t e0) {
   return FLETCHER_OK;
 }
 
+static int32_t launch_or_replay(Model* m, const int32_t* d_ids, const int32_t* lengths, int32_t B, int32_t pooling,
+                                float* d_out, int64_t T, int32_t n_tiles, int32_t max_len);
+
 static int32_t forward_device(Model* m, const int32_t* d_ids, const int32_t* lengths, int32_t B, int32_t pooling,
                               float* d_out) {
   Ctx* c = m->c;
@@ -370,6 +388,14 @@ static int32_t forward_device(Model* m, const int32_t* d_ids, const int32_t* len
   if ((rc = upload_meta(m, lengths, B, T, &n_tiles, &max_len))) return rc;
   if ((rc = ensure_rope(m, max_len))) return rc;
   m->last_T = T;
+  return launch_or_replay(m, d_ids, lengths, B, pooling, d_out, T, n_tiles, max_len);
+}
+
+// The kernel sequence of one forward pass (everything after the metadata upload).
+static int32_t run_layers(Model* m, const int32_t* d_ids, int32_t B, int32_t pooling, float* d_out, int64_t T,
+                          int32_t n_tiles, int32_t max_len) {
+  Ctx* c = m->c;
+  int32_t rc = 0;
   const int64_t H = m->H, I = m->I, Iup = m->Iup;
   const int32_t dt = m->dtype;
   const float eps = m->cfg.layer_norm_eps;
@@ -442,6 +468,71 @@ static int32_t forward_device(Model* m, const int32_t* d_ids, const int32_t* len
   FL_STAGE(FLETCHER_STAGE_POOL, launch_gather_rows_f32(c, dt, m->X, m->d_cu, B, H, m->d_cls));
   FL_STAGE(FLETCHER_STAGE_POOL, launch_sgemm(c, m->d_cls, H, m->wp, H, d_out, H, B, H, H, m->bp, FLETCHER_ACT_TANH));
 #undef FL_STAGE
+  return FLETCHER_OK;
+}
+
+// CUDA-graph replay of the kernel sequence for repeated batch shapes.  A shape (lengths,
+// pooling, input/output pointers) seen for the first time runs eagerly; the second time it is
+// captured; later calls replay the graph, which removes the per-kernel launch and tensor-map
+// encoding cost on the host (what dominates single-request latency).  The metadata upload
+// stays outside the graph, so replays read the freshly uploaded cu_seqlens / tile list.
+void clear_graphs(Model* m) {
+  for (auto& g : m->graphs) cudaGraphExecDestroy(g.exec);
+  m->graphs.clear();
+  m->graph_seen.clear();
+}
+
+static int32_t launch_or_replay(Model* m, const int32_t* d_ids, const int32_t* lengths, int32_t B, int32_t pooling,
+                                float* d_out, int64_t T, int32_t n_tiles, int32_t max_len) {
+  Ctx* c = m->c;
+  if (!m->use_graphs || m->timing) return run_layers(m, d_ids, B, pooling, d_out, T, n_tiles, max_len);
+  std::vector<int32_t> key;
+  key.reserve(B + 6);
+  const uint64_t pi = (uint64_t)(uintptr_t)d_ids, po = (uint64_t)(uintptr_t)d_out;
+  key.insert(key.end(), {pooling, B, (int32_t)pi, (int32_t)(pi >> 32), (int32_t)po, (int32_t)(po >> 32)});
+  key.insert(key.end(), lengths, lengths + B);
+  ++m->graph_tick;
+  for (auto& g : m->graphs)
+    if (g.key == key) {
+      g.last_use = m->graph_tick;
+      FL_CUDA(c, cudaGraphLaunch(g.exec, c->stream));
+      c->launches += g.kernels;
+      return FLETCHER_OK;
+    }
+  bool seen = false;
+  for (auto& k : m->graph_seen) seen |= k == key;
+  if (!seen) {
+    if (m->graph_seen.size() >= 64) m->graph_seen.erase(m->graph_seen.begin());
+    m->graph_seen.push_back(key);
+    return run_layers(m, d_ids, B, pooling, d_out, T, n_tiles, max_len);
+  }
+  const int64_t l0 = c->launches;
+  FL_CUDA(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  int32_t rc = run_layers(m, d_ids, B, pooling, d_out, T, n_tiles, max_len);
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  cudaGraphExec_t exec = nullptr;
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+  if (graph) cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {  // capture unavailable here: keep running eagerly
+    cudaGetLastError();
+    m->use_graphs = false;
+    c->launches = l0;
+    return run_layers(m, d_ids, B, pooling, d_out, T, n_tiles, max_len);
+  }
+  const int64_t kernels = c->launches - l0;
+  if (m->graphs.size() >= 16) {  // evict the least recently used
+    auto lru = std::min_element(m->graphs.begin(), m->graphs.end(),
+                                [](const Model::GraphEntry& a, const Model::GraphEntry& b) { return a.last_use < b.last_use; });
+    cudaGraphExecDestroy(lru->exec);
+    m->graphs.erase(lru);
+  }
+  m->graphs.push_back({key, exec, m->graph_tick, kernels});
+  FL_CUDA(c, cudaGraphLaunch(exec, c->stream));
   return FLETCHER_OK;
 }
 
@@ -567,6 +658,16 @@ int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count
   dev_free(c, tmp, count * 4);
   FL_CUDA(c, cudaStreamSynchronize(c->stream));
   return rc;
+}
+
+int32_t Cuda_Model_SetGraphs(CudaModelRef model, int32_t enable) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(m->c);
+  FL_CUDA(m->c, cudaStreamSynchronize(m->c->stream));
+  m->use_graphs = enable != 0;
+  clear_graphs(m);
+  return FLETCHER_OK;
 }
 
 int32_t Cuda_Model_SetStageTiming(CudaModelRef model, int32_t enable) {

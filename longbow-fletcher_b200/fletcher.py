@@ -84,6 +84,7 @@ def _sig(L):
         "Cuda_Model_ForwardBatchDevice": (i32, [vp, vp, i32p, i32, i32, vp]),
         "Cuda_Model_LastHidden": (i32, [vp, f32p, i64]),
         "Cuda_Model_SetStageTiming": (i32, [vp, i32]),
+        "Cuda_Model_SetGraphs": (i32, [vp, i32]),
         "Cuda_Model_StageTimes": (i32, [vp, f32p, i64p, i32]),
         "Cuda_GetLaunchCount": (i64, [vp]),
         "Cuda_Model_Free": (i32, [vp]),
@@ -314,6 +315,9 @@ class BertModel:
 
     STAGES = ["embed", "gemm_qkv", "rope", "attention", "gemm_o", "layernorm", "gemm_up", "activation",
               "gemm_down", "pool"]
+
+    def set_graphs(self, on: bool):
+        self.be.check(lib().Cuda_Model_SetGraphs(self.h, int(on)))
 
     def set_stage_timing(self, on: bool):
         self.be.check(lib().Cuda_Model_SetStageTiming(self.h, int(on)))
