@@ -38,9 +38,9 @@ sys.path[:0] = [os.path.join(ROOT, "longbow-fletcher_b200")]
 import synth  # noqa: E402
 
 METRIC = "embeddings/sec (nomic-embed-text seq512 bf16)"
-# ncu-measured DRAM traffic per launch of the tensor-core GEMMs (profiles/gemm_tc_cfg3.md),
-# bytes per launch, keyed by stage; None until captured.
-GEMM_TRAFFIC = None
+# ncu-measured DRAM traffic (read + write) of the four tensor-core GEMMs of one nomic layer, per
+# token (profiles/gemm_tc_cfg3.md: 1669 MB for 56.3K tokens).  Scaled to the timed forwards.
+GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 29640.0
 
 
 def peaks():
@@ -237,7 +237,13 @@ def main():
     achieved = gemm_flops / gemm_launches / (gemm_ms / gemm_launches / 1000) / 1e12
     roofline = {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05, all 4 GEMMs of every layer)",
                 "achieved": achieved, "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
-                "peak_source": f"{src} bf16_tflops_sustained", "traffic": GEMM_TRAFFIC,
+                "peak_source": f"{src} bf16_tflops_sustained",
+                "traffic": (GEMM_DRAM_BYTES_PER_TOKEN_LAYER * tok_ns * L / gemm_launches
+                            if cfg.hidden == 768 else None),
+                "traffic_note": "ncu dram__bytes_read+write per GEMM launch (profiles/gemm_tc_cfg3.md), "
+                                "per-token figure scaled to the timed forwards",
+                # activations in + out of the 4 GEMMs: reads 5H + I, writes 5H + I per token (16-bit)
+                "algorithmic_bytes_per_launch": 2.0 * tok_ns * L * (10 * Hh + 2 * I) / gemm_launches,
                 "flops_per_launch": gemm_flops / gemm_launches, "ms_per_launch": gemm_ms / gemm_launches}
     stage_ms = {k: v[0] / ns for k, v in st.items() if v[1]}
 
