@@ -274,22 +274,30 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int i = 0; i < BKV; i++)
             if (i >= valid) sv[i] = -INFINITY;
         }
-        float mx = m;
+        // Row max as a tree (8 independent chains, then a pairwise fold) to keep latency short.
+        float mp[8];
 #pragma unroll
-        for (int i = 0; i < BKV; i++) mx = fmaxf(mx, sv[i]);
+        for (int k = 0; k < 8; k++) mp[k] = fmaxf(sv[k], sv[8 + k]);
+#pragma unroll
+        for (int i = 16; i < BKV; i += 8)
+#pragma unroll
+          for (int k = 0; k < 8; k++) mp[k] = fmaxf(mp[k], sv[i + k]);
+        const float mx = fmaxf(m, fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                                         fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))));
         const float corr = ex2((m - mx) * sl2);
         const float ms = mx * sl2;
         m = mx;
         // P = exp2(S*scale*log2e - max) -> smem (row r, 64 keys = 128 B, 128-byte swizzle, K-major
         // for the PV MMA).  P buffer g&1 is free: PV_{g-2} finished before O_{g-2} was read.
-        float rs0 = 0.f, rs1 = 0.f;
+        float ra[4][2] = {};  // four independent packed partial sums
 #pragma unroll
         for (int i = 0; i < BKV; i += 2) {
           fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
           sv[i] = ex2(sv[i]);
           sv[i + 1] = ex2(sv[i + 1]);
-          add2(rs0, rs1, sv[i], sv[i + 1]);
+          add2(ra[(i >> 1) & 3][0], ra[(i >> 1) & 3][1], sv[i], sv[i + 1]);
         }
+        const float rsum = ((ra[0][0] + ra[0][1]) + (ra[1][0] + ra[1][1])) + ((ra[2][0] + ra[2][1]) + (ra[3][0] + ra[3][1]));
         uint8_t* prow = smem + OFF_P + b * P_BYTES + r * 128;
 #pragma unroll
         for (int c = 0; c < 8; c++) {
@@ -297,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           uint4 wv = make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
           *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = wv;
         }
-        l = l * corr + (rs0 + rs1);
+        l = l * corr + rsum;
         fence_async_smem();
         mbar_arrive(&p_full[b]);
         if (g >= 1) {  // O_{g-1} is ready once PV_{g-1} ran; that also frees P buffer (g-1)&1
