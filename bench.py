@@ -138,19 +138,77 @@ def run_reference(args, w, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_server_mix(args):
+    """cfg5: the server-batcher mix.  Requests of U{1..16} texts with lengths log-uniform in
+    [8, 512] arrive from `clients` closed-loop clients (each submits its next request when the
+    previous one returns); the batcher caps in-flight sequences at 16384 and dispatches batches
+    round-robin to one replica per GPU (embedder.Server).  One process drives all `--gpus` GPUs.
+    Reports sustained vectors/s and per-request latency (submit -> vectors on the host)."""
+    import concurrent.futures as cf
+    import threading
+
+    import embedder
+    cfg = synth.NOMIC
+    rng = np.random.default_rng(5)
+    reqs = []
+    for i in range(args.requests):
+        n = int(rng.integers(1, 17))
+        lens = np.exp(rng.uniform(np.log(8), np.log(513), size=n)).astype(np.int32).clip(8, 512)
+        reqs.append((synth.make_ids(lens, cfg.vocab_size, 9000 + i), lens))
+    emb = embedder.Embedder(cfg, synth.make_weights(cfg, 1), devices=range(args.gpus), dtype="bf16")
+    srv = embedder.Server(emb, max_in_flight=16384)
+    for r in reqs[:64]:  # warm-up: workspaces, kernels
+        srv.submit(*r).result()
+    lat, nxt, lock = [], [0], threading.Lock()
+
+    def client():
+        while True:
+            with lock:
+                i = nxt[0]
+                nxt[0] += 1
+            if i >= len(reqs):
+                return
+            _, t = srv.submit(*reqs[i]).result()
+            lat.append(t)
+
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(args.clients) as ex:
+        for f in [ex.submit(client) for _ in range(args.clients)]:
+            f.result()
+    wall = time.perf_counter() - t0
+    srv.close()
+    emb.close()
+    nvec = sum(len(r[1]) for r in reqs)
+    lat_ms = np.array(lat) * 1000
+    print(json.dumps({
+        "metric": "sustained embeddings/sec, server-batcher mix (nomic-embed-text bf16)", "value": nvec / wall,
+        "unit": "vectors/s", "n_gpus": args.gpus, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "cfg5: requests of U{1..16} texts, lengths log-uniform [8,512], <=16384 sequences "
+                               "in flight, round-robin over per-GPU replicas",
+                   "requests": args.requests, "clients": args.clients, "vectors": nvec},
+        "latency_ms": {"p50": float(np.percentile(lat_ms, 50)), "p99": float(np.percentile(lat_ms, 99))},
+        "wall_s": wall}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="fletcher", choices=["fletcher", "reference"])
-    ap.add_argument("--workload", default="cfg3", choices=sorted(synth.WORKLOADS))
+    ap.add_argument("--workload", default="cfg3", choices=sorted(synth.WORKLOADS) + ["cfg5"])
     ap.add_argument("--ref-sample", type=int, default=4, help="sequences per step for the CPU reference")
     ap.add_argument("--cpu-sample", type=int, default=8, help="sequences in the cpu_baseline sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--lat-iters", type=int, default=50, help="single-request latency samples")
+    ap.add_argument("--requests", type=int, default=20000, help="cfg5: requests in the sample")
+    ap.add_argument("--clients", type=int, default=256, help="cfg5: concurrent closed-loop clients")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "cfg5":
+        if int(os.environ.get("RANK", 0)) == 0:
+            run_server_mix(args)
+        return
     w = synth.WORKLOADS[args.workload]
 
     rank = int(os.environ.get("RANK", 0))

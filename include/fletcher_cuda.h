@@ -209,6 +209,11 @@ int64_t Cuda_Model_WeightCount(const FletcherBertConfig* cfg);
  * entries) and lengths in, host float32 out[numSeqs, hidden].  Synchronous. */
 int32_t Cuda_Model_ForwardBatch(CudaModelRef model, const int32_t* ids, const int32_t* lengths,
                                 int32_t numSeqs, int32_t pooling, float* out);
+/* Cuda_Model_ForwardBatch with the vectors returned as out_dtype (FLETCHER_F32, F16 or BF16;
+ * 16-bit values are rounded to nearest-even on the device, so half the bytes cross PCIe): the
+ * reference's fp16 transport, Cast(Float16) + ExtractBytes (embeddings.go:256-288). */
+int32_t Cuda_Model_ForwardBatchEx(CudaModelRef model, const int32_t* ids, const int32_t* lengths,
+                                  int32_t numSeqs, int32_t pooling, int32_t out_dtype, void* out);
 /* Same pass with device-resident ids (int32, packed) and a device float32 output; lengths
  * stay on the host (they shape the launch).  Asynchronous on the context's stream. */
 int32_t Cuda_Model_ForwardBatchDevice(CudaModelRef model, const int32_t* d_ids,

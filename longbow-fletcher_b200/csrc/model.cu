@@ -622,10 +622,16 @@ int32_t Cuda_Model_ForwardBatchDevice(CudaModelRef model, const int32_t* d_ids, 
 
 int32_t Cuda_Model_ForwardBatch(CudaModelRef model, const int32_t* ids, const int32_t* lengths, int32_t B,
                                 int32_t pooling, float* out) {
+  return Cuda_Model_ForwardBatchEx(model, ids, lengths, B, pooling, FLETCHER_F32, out);
+}
+
+int32_t Cuda_Model_ForwardBatchEx(CudaModelRef model, const int32_t* ids, const int32_t* lengths, int32_t B,
+                                  int32_t pooling, int32_t out_dtype, void* out) {
   Model* m = reinterpret_cast<Model*>(model);
   if (!m || !ids || !lengths || !out) return FLETCHER_ERR_INVALID;
   Ctx* c = m->c;
   DeviceGuard g(c);
+  FL_CHECK(c, out_dtype >= FLETCHER_F32 && out_dtype <= FLETCHER_BF16, "ForwardBatchEx: bad output dtype %d", out_dtype);
   FL_CHECK(c, B > 0, "ForwardBatch: empty batch");
   int64_t T = 0;
   for (int i = 0; i < B; i++) T += lengths[i] > 0 ? lengths[i] : 0;
@@ -636,7 +642,13 @@ int32_t Cuda_Model_ForwardBatch(CudaModelRef model, const int32_t* ids, const in
   if (rc) return rc;
   FL_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, T * 4, cudaMemcpyHostToDevice, c->stream));
   if ((rc = forward_device(m, m->d_ids, lengths, B, pooling, m->d_out))) return rc;
-  FL_CUDA(c, cudaMemcpyAsync(out, m->d_out, (int64_t)B * m->H * 4, cudaMemcpyDeviceToHost, c->stream));
+  const int64_t n = (int64_t)B * m->H;
+  if (out_dtype == FLETCHER_F32) {
+    FL_CUDA(c, cudaMemcpyAsync(out, m->d_out, n * 4, cudaMemcpyDeviceToHost, c->stream));
+  } else {  // cast on the device (round to nearest even), copy half the bytes
+    if ((rc = launch_cast(c, FLETCHER_F32, m->d_out, out_dtype, m->d_cls, n))) return rc;
+    FL_CUDA(c, cudaMemcpyAsync(out, m->d_cls, n * 2, cudaMemcpyDeviceToHost, c->stream));
+  }
   FL_CUDA(c, cudaStreamSynchronize(c->stream));
   return check_device_flag(c);
 }

@@ -82,6 +82,7 @@ def _sig(L):
         "Cuda_Model_WeightCount": (i64, [vp]),
         "Cuda_Model_ForwardBatch": (i32, [vp, i32p, i32p, i32, i32, f32p]),
         "Cuda_Model_ForwardBatchDevice": (i32, [vp, vp, i32p, i32, i32, vp]),
+        "Cuda_Model_ForwardBatchEx": (i32, [vp, i32p, i32p, i32, i32, i32, vp]),
         "Cuda_Model_LastHidden": (i32, [vp, f32p, i64]),
         "Cuda_Model_SetStageTiming": (i32, [vp, i32]),
         "Cuda_Model_SetGraphs": (i32, [vp, i32]),
@@ -306,6 +307,15 @@ class BertModel:
         lens = np.ascontiguousarray(lengths, np.int32)
         out = np.empty((lens.size, self.cfg.hidden), np.float32)
         self.be.check(lib().Cuda_Model_ForwardBatch(self.h, _i32p(ids), _i32p(lens), lens.size, pooling, _f32p(out)))
+        return out
+
+    def forward_batch_16(self, ids, lengths, pooling=POOL_MEAN_L2, out_dtype=F16):
+        """Vectors as float16 (or bfloat16 bit patterns in uint16) — the fp16 transport."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        lens = np.ascontiguousarray(lengths, np.int32)
+        out = np.empty((lens.size, self.cfg.hidden), np.float16 if out_dtype == F16 else np.uint16)
+        self.be.check(lib().Cuda_Model_ForwardBatchEx(self.h, _i32p(ids), _i32p(lens), lens.size, pooling, out_dtype,
+                                                      out.ctypes.data))
         return out
 
     def forward_batch_device(self, d_ids_ptr, lengths, pooling, d_out_ptr):

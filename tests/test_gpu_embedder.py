@@ -1,0 +1,55 @@
+"""GPU tests of the multi-replica embedder and the request batcher (embedder.py).  Two replicas
+share GPU 0 here; the split, batching and reassembly logic is the same as across GPUs."""
+import concurrent.futures as cf
+import dataclasses
+
+import numpy as np
+import pytest
+
+import synth
+
+pytestmark = pytest.mark.gpu
+
+CFG = dataclasses.replace(synth.NOMIC, num_layers=2)
+
+
+@pytest.fixture(scope="module")
+def emb():
+    import build
+    build.build()
+    import embedder
+    e = embedder.Embedder(CFG, synth.make_weights(CFG, 1), devices=[0, 0], dtype="bf16", max_batch=7,
+                          max_tokens=900)
+    yield e
+    e.close()
+
+
+def _direct(e, ids, lens):
+    m = e.replicas[0].model
+    return e.replicas[0].pool.submit(lambda: m.forward_batch(ids, lens, 1)).result()
+
+
+def test_embed_matches_single_replica(emb):
+    lens = synth.make_lengths(40, 8, 300, 5, "loguniform")
+    ids = synth.make_ids(lens, CFG.vocab_size, 5)
+    want = _direct(emb, ids, lens)
+    emb.replicas[0].throughput, emb.replicas[1].throughput = 3.0, 1.0  # uneven split
+    got = emb.embed(ids, lens)
+    assert np.array_equal(got, want)  # packing- and batching-invariant, bit for bit
+
+
+def test_server_requests(emb):
+    import embedder
+    srv = embedder.Server(emb, max_in_flight=64)
+    rng = np.random.default_rng(3)
+    reqs = []
+    for i in range(60):
+        lens = synth.make_lengths(int(rng.integers(1, 17)), 8, 200, 100 + i, "loguniform")
+        reqs.append((synth.make_ids(lens, CFG.vocab_size, 100 + i), lens))
+    with cf.ThreadPoolExecutor(8) as ex:
+        futs = list(ex.map(lambda r: srv.submit(*r), reqs))
+    srv.close()
+    for (ids, lens), f in zip(reqs, futs):
+        vecs, lat = f.result(timeout=60)
+        assert lat > 0 and vecs.shape == (len(lens), CFG.hidden)
+        assert np.array_equal(vecs, _direct(emb, ids, lens))

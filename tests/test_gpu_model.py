@@ -139,3 +139,40 @@ def test_graph_replay_matches_eager(be, dtype):
     for rep in range(4):  # first call eager, second captures, then replays
         for (i, l), want in zip(batches, eager):
             assert np.array_equal(m.forward_batch(i, l, 1), want), rep
+
+
+@pytest.mark.parametrize("out", ["f16", "bf16"])
+def test_16bit_output_transport(be, out):
+    """ForwardBatchEx returns the vectors rounded to 16 bits on the device: bit-identical to
+    rounding the float32 result on the host."""
+    import fletcher
+    from helpers import bf16_round
+    cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
+    m = model(be, cfg, "bf16", 1)
+    lens = np.array([50, 3, 129], np.int32)
+    ids = synth.make_ids(lens, cfg.vocab_size, 41)
+    f32 = m.forward_batch(ids, lens, 1)
+    if out == "f16":
+        assert np.array_equal(m.forward_batch_16(ids, lens, 1, fletcher.F16), f32.astype(np.float16))
+    else:
+        got = m.forward_batch_16(ids, lens, 1, fletcher.BF16)
+        assert np.array_equal((got.astype(np.uint32) << 16).view(np.float32), bf16_round(f32))
+
+
+def test_safetensors_checkpoint_end_to_end(be, tmp_path, oracle_mod):
+    """A BF16 SafeTensors checkpoint (HF names, (out, in) Linear weights) loads through the
+    ingest path and embeds like the oracle on the same (bf16-rounded) weights."""
+    import fletcher
+    import weights
+    cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
+    blob = synth.make_weights(cfg, 1)
+    p = tmp_path / "nomic2.safetensors"
+    weights.write_safetensors(str(p), weights.safetensors_from_blob(blob, cfg), "BF16")
+    loaded = weights.blob_from_safetensors(str(p), cfg)
+    m = fletcher.BertModel(be, cfg, "bf16")
+    m.load_raw(loaded)
+    lens = np.array([77, 20], np.int32)
+    ids = synth.make_ids(lens, cfg.vocab_size, 13)
+    want = oracle_mod.forward(cfg, loaded, ids, lens)["mean"]
+    assert_close_16(m.forward_batch(ids, lens, 1), want, "safetensors bf16")
+    m.close()
