@@ -52,13 +52,6 @@ int32_t launch_attention_f32(Ctx* c, const float* q, const float* k, const float
                              float* out, int64_t ld_out, const int32_t* cu_seqlens, int32_t B,
                              int64_t T, int32_t nh, int32_t dh, float scale, int32_t max_len);
 
-// bf16/f16 flash attention, head_dim 64.  q/k/v rows have stride ld_in elements (for a packed
-// [T, 3H] QKV buffer: q = qkv, k = qkv + H, v = qkv + 2H, ld_in = 3H).
-// tiles: int2 {seq, q_row_start} per 64-row query tile.
-int32_t launch_flash_attention_ld(Ctx* c, int32_t dtype, const void* q, const void* k, const void* v,
-                                  int64_t ld_in, void* out, int64_t ld_out, const int32_t* cu_seqlens,
-                                  const int2* tiles, int32_t num_tiles, int32_t nh, float scale);
-
 // bf16/f16 flash attention on tcgen05 (attention_tc.cu), head_dim 64: q/k/v [T, H] views with
 // row stride ld_in; tiles128: int2 {seq, q_row_start} per 128-row query tile.
 int32_t launch_flash_attention_tc(Ctx* c, int32_t dtype, const void* q, const void* k, const void* v,
