@@ -3,7 +3,7 @@
 //
 // Per layer (16-bit mode), 7 launches:
 //   QKV   = X . Wqkv^T (+b), RoPE on Q|K in the epilogue          (tcgen05 GEMM, EPI_ROPE)
-//   CTX   = flash-attention(QKV) over packed sequences            (mma.sync flash kernel)
+//   CTX   = flash-attention(QKV) over packed sequences            (tcgen05 attention)
 //   S     = CTX . Wo^T + bo + X                                   (tcgen05 GEMM, EPI_RESIDUAL)
 //   X     = LayerNorm(S)                                          (warp-per-row LN)
 //   ACT   = SwiGLU / GeluFast(X . Wi^T + bi)                      (tcgen05 GEMM, EPI_SWIGLU/GELU)
@@ -11,7 +11,8 @@
 //   X     = LayerNorm(S)
 // fp32 mode runs the same graph with the SIMT GEMM, a RoPE kernel and the fp32 attention
 // kernel, using the reference's fast-math formulas, for parity with its CPU path.
-// The residual stream X stays in the model dtype; LayerNorm statistics are fp32.
+// The residual stream X stays in the model dtype; LayerNorm statistics are fp32.  The kernel
+// sequence is captured into a CUDA graph for repeated batch shapes.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
