@@ -5,20 +5,23 @@
 // (cpu_backend.go:662-758): per sequence and head, O = softmax(scale * Q K^T) V, keys limited to
 // the sequence (cu_seqlens).
 //
-// Persistent kernel: each CTA walks work items w = (128-query tile, head) in a strided order
-// (tiles come longest-sequence first).  The three roles run through one continuous sequence of
-// 64-key blocks g across all of the CTA's work items, so the next item's Q load and first
-// Q K^T overlap the previous item's tail.  192 threads:
-//   warp 0    : TMA producer — Q tile per work item (2 buffers), K and V blocks (2-stage ring);
-//   warp 1    : MMA issuer — S_g = Q K_g^T (M=128, N=64, K=64) into TMEM S buffer g&1, and
-//               O_g = P_g V_g (M=128, N=64, K=64 keys; V read MN-major straight from its TMA
-//               tile) into TMEM O buffer g&1; S_{g+1} is issued before waiting for P_g;
-//   warps 2-5 : softmax — thread = query row: tcgen05.ld its S row, mask keys past the
-//               sequence end, online max / exp2 / row sum, write P (16-bit) to 128B-swizzled
-//               smem for the PV MMA, accumulate O_g from TMEM into fp32 registers with the exact
-//               rescale exp2((m_old - m_new) * scale * log2 e), and store finished rows.
-// TMEM: 2 x 64 (S) + 2 x 64 (O) = 256 columns; ~97 KB smem -> two CTAs per SM.
-// All mbarrier waits are bounded (device error flag + abort, as in the GEMM).  No multicast.
+// Persistent kernel, two query-tile slots per CTA and two CTAs per SM.  Each slot walks its own
+// work items w = (128-query tile, head) in a strided order (tiles come longest-sequence first)
+// through 64-key blocks.  320 threads:
+//   warp 0    : TMA producer for both slots — Q tile per work item, K and V blocks (2-stage ring
+//               per slot); polls the slots' barriers and issues whichever load is free;
+//   warp 1    : MMA issuer for both slots (polling likewise) — S_j = Q K_j^T (M=128, N=64, K=64)
+//               into the slot's TMEM S columns, then O += P_j V_j with P_j read from TMEM (A
+//               operand) and V_j MN-major straight from its TMA tile.  tcgen05.mma runs in issue
+//               order, so S_{j+1} may overwrite P_j's columns once PV_j has been issued;
+//   warps 2-5 : softmax of slot 0, warps 6-9 softmax of slot 1 — thread = query row: tcgen05.ld
+//               its S row, mask keys past the sequence end, exp2 against a lazily updated
+//               reference max, and tcgen05.st P (16-bit pairs) over the upper half of S.  The
+//               reference max moves only when a row's block max exceeds it by more than 2^8 in
+//               exp2 terms; then O (complete, because S_j's commit follows PV_{j-1}) is rescaled
+//               in TMEM.  At the end of an item the row of O is divided by its sum and stored.
+// TMEM per slot: S/P 64 columns + O 64 columns; 256 per CTA.  ~98 KB smem.  All mbarrier waits
+// are bounded (device error flag + abort, as in the GEMM).  No multicast.
 #include "tc_common.cuh"
 
 namespace fl {
@@ -27,17 +30,18 @@ namespace tca {
 using namespace tc;
 
 constexpr int BQ = 128, BKV = 64, D = 64;
-constexpr int kThreads = 192;
+constexpr int kSlots = 2;
+constexpr int kThreads = 64 + kSlots * 128;
 constexpr int Q_BYTES = BQ * D * 2;
 constexpr int KV_BYTES = BKV * D * 2;
-constexpr int P_BYTES = BQ * BKV * 2;
-constexpr int OFF_Q = 0;  // 2 buffers
-constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
-constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
-constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-constexpr int SMEM = OFF_BAR + 256 + 1024;
-constexpr int TMEM_COLS = 256;  // S0 [0,64) S1 [64,128) O0 [128,192) O1 [192,256)
+// Per slot: Q, K[2], V[2] (each 1024-byte aligned).
+constexpr int SLOT_Q = 0, SLOT_K = Q_BYTES, SLOT_V = Q_BYTES + 2 * KV_BYTES;
+constexpr int SLOT_BYTES = Q_BYTES + 4 * KV_BYTES;
+constexpr int kBarsPerSlot = 10;
+constexpr int OFF_BAR = kSlots * SLOT_BYTES;
+constexpr int SMEM = OFF_BAR + kSlots * kBarsPerSlot * 8 + 16 + 1024;
+constexpr int TMEM_COLS = 256;  // slot s: S [128s, 128s+64) with P in its upper 32 columns, O [128s+64, 128s+128)
+constexpr float kRescaleLog2 = 8.0f;  // P <= 2^8 between reference-max updates
 
 struct AttnArgs {
   const int32_t* cu;
@@ -54,11 +58,24 @@ struct Work {
   int start, L, q0, h, nb;
 };
 
+// Barriers of one slot.
+struct SlotBars {
+  uint64_t *q_full, *q_empty, *kv_full, *kv_empty, *s_full, *p_full, *o_full, *o_free;
+  __device__ SlotBars(uint64_t* b)
+      : q_full(b), q_empty(b + 1), kv_full(b + 2), kv_empty(b + 4), s_full(b + 6), p_full(b + 7), o_full(b + 8),
+        o_free(b + 9) {}
+};
+
 // 2^x on the SFU (one instruction; -inf -> 0).
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 // Packed two-lane fp32 FMA / add (sm_100): one instruction for two values.
 __device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
@@ -72,6 +89,25 @@ __device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1) {
       " mov.b64 {%0, %1}, d;\n}"
       : "+f"(d0), "+f"(d1)
       : "f"(a0), "f"(a1));
+}
+// Keys at and past `valid` lie outside the sequence.
+__device__ __forceinline__ void mask_tail(float (&sv)[BKV], int valid) {
+#pragma unroll
+  for (int i = 0; i < BKV; i++)
+    if (i >= valid) sv[i] = -INFINITY;
+}
+// Row max as a short tree of 3-input max instructions.
+__device__ __forceinline__ float row_max(const float (&sv)[BKV]) {
+  float mp[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) mp[k] = max3(sv[k], sv[8 + k], sv[16 + k]);
+#pragma unroll
+  for (int k = 0; k < 8; k++) mp[k] = max3(mp[k], sv[24 + k], sv[32 + k]);
+#pragma unroll
+  for (int k = 0; k < 8; k++) mp[k] = max3(mp[k], sv[40 + k], sv[48 + k]);
+#pragma unroll
+  for (int k = 0; k < 8; k++) mp[k] = fmaxf(mp[k], sv[56 + k]);
+  return max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
 }
 
 __device__ __forceinline__ Work decode(const AttnArgs& a, int w) {
@@ -97,19 +133,39 @@ __device__ __forceinline__ uint64_t sw128_desc_mn(uint32_t saddr) {
   return d;
 }
 
-template <typename T>
-__device__ __forceinline__ void store_row(const AttnArgs& a, const Work& wk, int r, const float (&o)[D], float l) {
-  if (wk.q0 + r >= wk.L) return;
-  const float inv = 1.0f / l;
-  T* dst = reinterpret_cast<T*>(a.out) + (int64_t)(wk.start + wk.q0 + r) * a.ld_out + wk.h * D;
-#pragma unroll
-  for (int c = 0; c < 8; c++) {
-    const float* v = &o[c * 8];
-    reinterpret_cast<uint4*>(dst)[c] =
-        make_uint4(pack2<T>(v[0] * inv, v[1] * inv), pack2<T>(v[2] * inv, v[3] * inv),
-                   pack2<T>(v[4] * inv, v[5] * inv), pack2<T>(v[6] * inv, v[7] * inv));
+// Bookkeeping that a polling thread (TMA or MMA) keeps per slot.
+struct SlotCursor {
+  int w;       // current work item (>= num_work: slot finished)
+  Work wk;
+  int j;       // next block of the item
+  uint32_t t;  // items started by this slot
+  uint32_t g;  // K/V blocks consumed by this slot (ring stage g & 1)
+  int phase;   // producer: 0 = Q next, 1 = K/V next; MMA: 0 = S_j next, 1 = PV_j next
+};
+
+// Poll-loop watchdog: returns false (after flagging a timeout) when nothing progressed for
+// ~2 s or another role aborted.
+struct Watchdog {
+  long long last;
+  uint32_t idle;
+  __device__ __forceinline__ bool tick(bool progress, volatile int* abort, int32_t* err) {
+    if (progress) {
+      idle = 0;
+      last = clock64();
+      return true;
+    }
+    __nanosleep(32);
+    if ((++idle & 63) == 0) {
+      if (*abort) return false;
+      if (clock64() - last > kWaitLimitCycles) {
+        atomicExch(err, kDevWaitTimeout);
+        *abort = 1;
+        return false;
+      }
+    }
+    return true;
   }
-}
+};
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -119,31 +175,25 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* q_full = bars;         // [2]
-  uint64_t* q_empty = bars + 2;    // [2]
-  uint64_t* kv_full = bars + 4;    // [2]
-  uint64_t* kv_empty = bars + 6;   // [2]
-  uint64_t* s_full = bars + 8;     // [2]
-  uint64_t* s_free = bars + 10;    // [2]
-  uint64_t* p_full = bars + 12;    // [2]
-  uint64_t* o_full = bars + 14;    // [2]
-  uint64_t* o_free = bars + 16;    // [2]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 18);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kSlots * kBarsPerSlot);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int vstride = gridDim.x * kSlots;  // virtual slots in the grid
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; i++) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 128);
+    for (int s = 0; s < kSlots; s++) {
+      SlotBars B(bars + s * kBarsPerSlot);
+      mbar_init(B.q_full, 1);
+      mbar_init(B.q_empty, 1);
+      for (int i = 0; i < 2; i++) {
+        mbar_init(&B.kv_full[i], 1);
+        mbar_init(&B.kv_empty[i], 1);
+      }
+      mbar_init(B.s_full, 1);
+      mbar_init(B.p_full, 128);
+      mbar_init(B.o_full, 1);
+      mbar_init(B.o_free, 128);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -166,187 +216,187 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 0) {
     if (lane == 0) {
-      int g = 0, t = 0;
-      for (int w = blockIdx.x; w < args.num_work; w += gridDim.x, ++t) {
-        const Work wk = decode(args, w);
-        const int qb = t & 1;
-        if (!mbar_wait(&q_empty[qb], ((t >> 1) & 1) ^ 1, abort, args.err)) break;
-        mbar_expect_tx(&q_full[qb], Q_BYTES);
-        tma_load_2d(smem + OFF_Q + qb * Q_BYTES, &tmQ, &q_full[qb], wk.h * D, wk.start + wk.q0);
-        bool ok = true;
-        for (int j = 0; j < wk.nb; j++, g++) {
-          const int b = g & 1;
-          if (!mbar_wait(&kv_empty[b], ((g >> 1) & 1) ^ 1, abort, args.err)) {
-            ok = false;
-            break;
+      SlotCursor cs[kSlots];
+      for (int s = 0; s < kSlots; s++) {
+        cs[s] = SlotCursor{(int)blockIdx.x * kSlots + s, Work{}, 0, 0, 0, 0};
+        if (cs[s].w < args.num_work) cs[s].wk = decode(args, cs[s].w);
+      }
+      Watchdog wd{clock64(), 0};
+      for (;;) {
+        bool active = false, progress = false;
+#pragma unroll
+        for (int s = 0; s < kSlots; s++) {
+          SlotCursor& c = cs[s];
+          if (c.w >= args.num_work) continue;
+          active = true;
+          SlotBars B(bars + s * kBarsPerSlot);
+          uint8_t* sb = smem + s * SLOT_BYTES;
+          if (c.phase == 0) {
+            if (!mbar_test(B.q_empty, (c.t & 1) ^ 1)) continue;
+            mbar_expect_tx(B.q_full, Q_BYTES);
+            tma_load_2d(sb + SLOT_Q, &tmQ, B.q_full, c.wk.h * D, c.wk.start + c.wk.q0);
+            c.phase = 1;
+            progress = true;
           }
-          mbar_expect_tx(&kv_full[b], 2 * KV_BYTES);
-          tma_load_2d(smem + OFF_K + b * KV_BYTES, &tmK, &kv_full[b], wk.h * D, wk.start + j * BKV);
-          tma_load_2d(smem + OFF_V + b * KV_BYTES, &tmV, &kv_full[b], wk.h * D, wk.start + j * BKV);
+          const int b = c.g & 1;
+          if (!mbar_test(&B.kv_empty[b], ((c.g >> 1) & 1) ^ 1)) continue;
+          mbar_expect_tx(&B.kv_full[b], 2 * KV_BYTES);
+          tma_load_2d(sb + SLOT_K + b * KV_BYTES, &tmK, &B.kv_full[b], c.wk.h * D, c.wk.start + c.j * BKV);
+          tma_load_2d(sb + SLOT_V + b * KV_BYTES, &tmV, &B.kv_full[b], c.wk.h * D, c.wk.start + c.j * BKV);
+          progress = true;
+          c.g++;
+          if (++c.j == c.wk.nb) {
+            c.j = 0;
+            c.t++;
+            c.phase = 0;
+            c.w += vstride;
+            if (c.w < args.num_work) c.wk = decode(args, c.w);
+          }
         }
-        if (!ok) break;
+        if (!active || !wd.tick(progress, abort, args.err)) break;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t id_s = idesc<T, BQ, BKV>();
       const uint32_t id_o = idesc<T, BQ, D, true>();
-      // O_i = P_i V_i for block i (buffers i&1).
-      auto issue_pv = [&](int i) -> bool {
-        const int b = i & 1;
-        if (!mbar_wait(&p_full[b], (i >> 1) & 1, abort, args.err)) return false;
-        if (!mbar_wait(&o_free[b], ((i >> 1) & 1) ^ 1, abort, args.err)) return false;
-        tc_fence_after();
-        const uint64_t p_desc = sw128_desc(smem_u32(smem + OFF_P + b * P_BYTES));
-        const uint64_t v_desc = sw128_desc_mn(smem_u32(smem + OFF_V + b * KV_BYTES));
+      SlotCursor cs[kSlots];
+      uint32_t gs[kSlots];  // blocks completed by the slot (s_full / p_full phases)
+      for (int s = 0; s < kSlots; s++) {
+        cs[s] = SlotCursor{(int)blockIdx.x * kSlots + s, Work{}, 0, 0, 0, 0};
+        gs[s] = 0;
+        if (cs[s].w < args.num_work) cs[s].wk = decode(args, cs[s].w);
+      }
+      Watchdog wd{clock64(), 0};
+      for (;;) {
+        bool active = false, progress = false;
 #pragma unroll
-        for (int k = 0; k < BKV / 16; k++)  // 16 keys per step: +32 B in P's K-major atom, +2 KB in V
-          mma_f16(tmem + 2 * BKV + b * D, p_desc + 2 * k, v_desc + (uint64_t)k * (2048 >> 4), id_o, k > 0);
-        mma_commit(&o_full[b]);
-        mma_commit(&kv_empty[b]);
-        return true;
-      };
-      int g = 0, t = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x, ++t) {
-        const Work wk = decode(args, w);
-        const int qb = t & 1;
-        if (!mbar_wait(&q_full[qb], (t >> 1) & 1, abort, args.err)) break;
-        const uint64_t q_desc = sw128_desc(smem_u32(smem + OFF_Q + qb * Q_BYTES));
-        for (int j = 0; j < wk.nb; j++, g++) {
-          const int b = g & 1;
-          if (!mbar_wait(&kv_full[b], (g >> 1) & 1, abort, args.err) ||
-              !mbar_wait(&s_free[b], ((g >> 1) & 1) ^ 1, abort, args.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t k_desc = sw128_desc(smem_u32(smem + OFF_K + b * KV_BYTES));
+        for (int s = 0; s < kSlots; s++) {
+          SlotCursor& c = cs[s];
+          if (c.w >= args.num_work) continue;
+          active = true;
+          SlotBars B(bars + s * kBarsPerSlot);
+          uint8_t* sb = smem + s * SLOT_BYTES;
+          const uint32_t t_s = tmem + s * 128, t_p = t_s + 32, t_o = t_s + 64;
+          const int b = c.g & 1;
+          if (c.phase == 0) {  // S_j = Q K_j^T
+            if (c.j == 0 && !mbar_test(B.q_full, c.t & 1)) continue;
+            if (!mbar_test(&B.kv_full[b], (c.g >> 1) & 1)) continue;
+            tc_fence_after();
+            const uint64_t q_desc = sw128_desc(smem_u32(sb + SLOT_Q));
+            const uint64_t k_desc = sw128_desc(smem_u32(sb + SLOT_K + b * KV_BYTES));
 #pragma unroll
-          for (int k = 0; k < D / 16; k++) mma_f16(tmem + b * BKV, q_desc + 2 * k, k_desc + 2 * k, id_s, k > 0);
-          mma_commit(&s_full[b]);
-          if (j == wk.nb - 1) mma_commit(&q_empty[qb]);  // Q buffer free once these MMAs finish
-          if (g >= 1 && !issue_pv(g - 1)) {
-            ok = false;
-            break;
+            for (int k = 0; k < D / 16; k++) mma_f16(t_s, q_desc + 2 * k, k_desc + 2 * k, id_s, k > 0);
+            mma_commit(B.s_full);
+            if (c.j == c.wk.nb - 1) mma_commit(B.q_empty);  // Q free once the item's last S ran
+            c.phase = 1;
+            progress = true;
+          } else {  // O += P_j V_j
+            if (!mbar_test(B.p_full, gs[s] & 1)) continue;
+            if (c.j == 0 && !mbar_test(B.o_free, (c.t & 1) ^ 1)) continue;  // previous item's O read
+            tc_fence_after();
+            const uint64_t v_desc = sw128_desc_mn(smem_u32(sb + SLOT_V + b * KV_BYTES));
+#pragma unroll
+            for (int k = 0; k < BKV / 16; k++)  // 16 keys per step: 8 TMEM columns of P, +2 KB in V
+              mma_f16_ts(t_o, t_p + 8 * k, v_desc + (uint64_t)k * (2048 >> 4), id_o, (c.j > 0 || k > 0) ? 1u : 0u);
+            mma_commit(&B.kv_empty[b]);
+            gs[s]++;
+            c.g++;
+            c.phase = 0;
+            progress = true;
+            if (++c.j == c.wk.nb) {
+              mma_commit(B.o_full);
+              c.j = 0;
+              c.t++;
+              c.w += vstride;
+              if (c.w < args.num_work) c.wk = decode(args, c.w);
+            }
           }
         }
+        if (!active || !wd.tick(progress, abort, args.err)) break;
       }
-      if (ok && g >= 1) issue_pv(g - 1);
     }
   } else {
+    const int s = (warp - 2) >> 2;
     const int q = warp & 3;
     const int r = q * 32 + lane;  // query row within the tile
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    SlotBars B(bars + s * kBarsPerSlot);
+    const uint32_t t_s = tmem + ((uint32_t)(q * 32) << 16) + s * 128, t_p = t_s + 32, t_o = t_s + 64;
     const float sl2 = args.sl2;
-    float o[D];
-#pragma unroll
-    for (int i = 0; i < D; i++) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, m_o = -INFINITY;
-    Work prev{};
-    int g = 0;
-    bool ok = true;
-    for (int w = blockIdx.x; w < args.num_work && ok; w += gridDim.x) {
+    uint32_t gs = 0, t = 0;
+    for (int w = blockIdx.x * kSlots + s; w < args.num_work; w += vstride, ++t) {
       const Work wk = decode(args, w);
-      for (int j = 0; j < wk.nb; j++, g++) {
-        const int b = g & 1;
-        if (!mbar_wait(&s_full[b], (g >> 1) & 1, abort, args.err)) {
+      float m_ref = 0.f, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < wk.nb; j++, gs++) {
+        if (!mbar_wait(B.s_full, gs & 1, abort, args.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int kbase = j * BKV;
-        const int valid = wk.L - kbase;  // keys of this block inside the sequence (>= 1)
-        // m_pb: the max that P_{g-1} was computed with; l_prev: finished row sum of the previous item.
-        const float m_pb = m;
-        const float l_prev = l;
-        if (j == 0) {
-          m = -INFINITY;
-          l = 0.f;
-        }
-        // The block's S row (one 64-column TMEM load), masked past the sequence end.
         float sv[BKV];
-        tmem_ld64(tmem + lane_off + b * BKV, sv);
-        tc_fence_before();
-        mbar_arrive(&s_free[b]);
-        if (valid < BKV) {  // only a sequence's last block needs the key mask
+        tmem_ld64(t_s, sv);
+        const int valid = wk.L - j * BKV;  // keys of this block inside the sequence (>= 1)
+        if (valid < BKV) mask_tail(sv, valid);
+        const float mx = row_max(sv);
+        if (j == 0) {
+          m_ref = mx;
+        } else {
+          const bool need = (mx - m_ref) * sl2 > kRescaleLog2;
+          if (__any_sync(0xffffffffu, need)) {
+            // Rare path.  O holds PV_0..PV_{j-1} complete (S_j's commit came after PV_{j-1});
+            // the S row is reloaded afterwards so that it is not live across the rescale.
+            const float f = need ? ex2((m_ref - mx) * sl2) : 1.0f;
+            if (need) {
+              m_ref = mx;
+              l *= f;
+            }
+#pragma unroll 1
+            for (int hh = 0; hh < 2; hh++) {
+              float ov[32];
+              tmem_ld32(t_o + hh * 32, ov);
+              uint32_t ou[32];
 #pragma unroll
-          for (int i = 0; i < BKV; i++)
-            if (i >= valid) sv[i] = -INFINITY;
+              for (int c = 0; c < 32; c++) ou[c] = __float_as_uint(ov[c] * f);
+              tmem_st32(t_o + hh * 32, ou);
+            }
+            tmem_ld64(t_s, sv);
+            if (valid < BKV) mask_tail(sv, valid);
+          }
         }
-        // Row max as a tree (8 independent chains, then a pairwise fold) to keep latency short.
-        float mp[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) mp[k] = fmaxf(sv[k], sv[8 + k]);
-#pragma unroll
-        for (int i = 16; i < BKV; i += 8)
-#pragma unroll
-          for (int k = 0; k < 8; k++) mp[k] = fmaxf(mp[k], sv[i + k]);
-        const float mx = fmaxf(m, fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                                         fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))));
-        const float corr = ex2((m - mx) * sl2);
-        const float ms = mx * sl2;
-        m = mx;
-        // P = exp2(S*scale*log2e - max) -> smem (row r, 64 keys = 128 B, 128-byte swizzle, K-major
-        // for the PV MMA).  P buffer g&1 is free: PV_{g-2} finished before O_{g-2} was read.
+        const float ms = m_ref * sl2;
         float ra[4][2] = {};  // four independent packed partial sums
+        uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < BKV; i += 2) {
           fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
           sv[i] = ex2(sv[i]);
           sv[i + 1] = ex2(sv[i + 1]);
           add2(ra[(i >> 1) & 3][0], ra[(i >> 1) & 3][1], sv[i], sv[i + 1]);
+          pk[i >> 1] = pack2<T>(sv[i], sv[i + 1]);
         }
-        const float rsum = ((ra[0][0] + ra[0][1]) + (ra[1][0] + ra[1][1])) + ((ra[2][0] + ra[2][1]) + (ra[3][0] + ra[3][1]));
-        uint8_t* prow = smem + OFF_P + b * P_BYTES + r * 128;
+        tmem_st32(t_p, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(B.p_full);
+        l += ((ra[0][0] + ra[0][1]) + (ra[1][0] + ra[1][1])) + ((ra[2][0] + ra[2][1]) + (ra[3][0] + ra[3][1]));
+      }
+      if (!ok || !mbar_wait(B.o_full, t & 1, abort, args.err)) break;
+      tc_fence_after();
+      float o[D];
+      tmem_ld64(t_o, o);
+      tc_fence_before();
+      mbar_arrive(B.o_free);
+      if (wk.q0 + r < wk.L) {
+        const float inv = 1.0f / l;
+        T* dst = reinterpret_cast<T*>(args.out) + (int64_t)(wk.start + wk.q0 + r) * args.ld_out + wk.h * D;
 #pragma unroll
         for (int c = 0; c < 8; c++) {
-          const float* v = &sv[c * 8];
-          uint4 wv = make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
-          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = wv;
+          const float* v = &o[c * 8];
+          reinterpret_cast<uint4*>(dst)[c] =
+              make_uint4(pack2<T>(v[0] * inv, v[1] * inv), pack2<T>(v[2] * inv, v[3] * inv),
+                         pack2<T>(v[4] * inv, v[5] * inv), pack2<T>(v[6] * inv, v[7] * inv));
         }
-        l = l * corr + rsum;
-        fence_async_smem();
-        mbar_arrive(&p_full[b]);
-        if (g >= 1) {  // O_{g-1} is ready once PV_{g-1} ran; that also frees P buffer (g-1)&1
-          const int i = g - 1, bo = i & 1;
-          if (!mbar_wait(&o_full[bo], (i >> 1) & 1, abort, args.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const float f = exp2f((m_o - m_pb) * sl2);
-          {
-            float tt[D];
-            tmem_ld64(tmem + lane_off + 2 * BKV + bo * D, tt);
-#pragma unroll
-            for (int c = 0; c < D; c += 2) fma2(o[c], o[c + 1], o[c], o[c + 1], f, f, tt[c], tt[c + 1]);
-          }
-          tc_fence_before();
-          mbar_arrive(&o_free[bo]);
-          m_o = m_pb;
-          if (j == 0) {  // block g-1 closed the previous work item
-            store_row<T>(args, prev, r, o, l_prev);
-#pragma unroll
-            for (int c = 0; c < D; c++) o[c] = 0.f;
-            m_o = -INFINITY;
-          }
-        }
-      }
-      prev = wk;
-    }
-    if (ok && g >= 1) {
-      const int i = g - 1, bo = i & 1;
-      if (mbar_wait(&o_full[bo], (i >> 1) & 1, abort, args.err)) {
-        tc_fence_after();
-        const float f = exp2f((m_o - m) * sl2);
-        {
-          float tt[D];
-          tmem_ld64(tmem + lane_off + 2 * BKV + bo * D, tt);
-#pragma unroll
-          for (int c = 0; c < D; c += 2) fma2(o[c], o[c + 1], o[c], o[c + 1], f, f, tt[c], tt[c + 1]);
-        }
-        store_row<T>(args, prev, r, o, l);
       }
     }
   }
@@ -390,7 +440,8 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void*
       FL_CUDA(c, cudaFuncSetAttribute(k_attn_tc<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     attr_set[ti][c->device & 63] = true;
   }
-  const int grid = work < 2 * c->num_sms ? work : 2 * c->num_sms;
+  const int want = (work + kSlots - 1) / kSlots;
+  const int grid = want < 2 * c->num_sms ? want : 2 * c->num_sms;
   if (dt == FLETCHER_BF16)
     k_attn_tc<__nv_bfloat16><<<grid, kThreads, SMEM, c->stream>>>(mq, mk, mv, a);
   else
