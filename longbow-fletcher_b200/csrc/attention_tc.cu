@@ -8,9 +8,9 @@
 // Persistent kernel, two query-tile slots per CTA and two CTAs per SM.  Each slot walks its own
 // work items w = (128-query tile, head) in a strided order (tiles come longest-sequence first)
 // through 64-key blocks.  320 threads:
-//   warp 0    : TMA producer for both slots — Q tile per work item, K and V blocks (2-stage ring
-//               per slot); polls the slots' barriers and issues whichever load is free;
-//   warp 1    : MMA issuer for both slots (polling likewise) — S_j = Q K_j^T (M=128, N=64, K=64)
+//   warps 0-1 : control thread of slot 0 / slot 1 — TMA loads (Q tile per work item, K and V
+//               blocks in a 2-stage ring; the next item's Q and first block are fetched during
+//               the current item's last block) and MMA issue: S_j = Q K_j^T (M=128, N=64, K=64)
 //               into the slot's TMEM S columns, then O += P_j V_j with P_j read from TMEM (A
 //               operand) and V_j MN-major straight from its TMA tile.  tcgen05.mma runs in issue
 //               order, so S_{j+1} may overwrite P_j's columns once PV_j has been issued;
@@ -133,40 +133,6 @@ __device__ __forceinline__ uint64_t sw128_desc_mn(uint32_t saddr) {
   return d;
 }
 
-// Bookkeeping that a polling thread (TMA or MMA) keeps per slot.
-struct SlotCursor {
-  int w;       // current work item (>= num_work: slot finished)
-  Work wk;
-  int j;       // next block of the item
-  uint32_t t;  // items started by this slot
-  uint32_t g;  // K/V blocks consumed by this slot (ring stage g & 1)
-  int phase;   // producer: 0 = Q next, 1 = K/V next; MMA: 0 = S_j next, 1 = PV_j next
-};
-
-// Poll-loop watchdog: returns false (after flagging a timeout) when nothing progressed for
-// ~2 s or another role aborted.
-struct Watchdog {
-  long long last;
-  uint32_t idle;
-  __device__ __forceinline__ bool tick(bool progress, volatile int* abort, int32_t* err) {
-    if (progress) {
-      idle = 0;
-      last = clock64();
-      return true;
-    }
-    __nanosleep(32);
-    if ((++idle & 63) == 0) {
-      if (*abort) return false;
-      if (clock64() - last > kWaitLimitCycles) {
-        atomicExch(err, kDevWaitTimeout);
-        *abort = 1;
-        return false;
-      }
-    }
-    return true;
-  }
-};
-
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -214,106 +180,84 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 0) {
+  if (warp < kSlots) {
+    // Control thread of slot `warp`: TMA loads and MMA issue with sleeping bounded waits.
     if (lane == 0) {
-      SlotCursor cs[kSlots];
-      for (int s = 0; s < kSlots; s++) {
-        cs[s] = SlotCursor{(int)blockIdx.x * kSlots + s, Work{}, 0, 0, 0, 0};
-        if (cs[s].w < args.num_work) cs[s].wk = decode(args, cs[s].w);
-      }
-      Watchdog wd{clock64(), 0};
-      for (;;) {
-        bool active = false, progress = false;
-#pragma unroll
-        for (int s = 0; s < kSlots; s++) {
-          SlotCursor& c = cs[s];
-          if (c.w >= args.num_work) continue;
-          active = true;
-          SlotBars B(bars + s * kBarsPerSlot);
-          uint8_t* sb = smem + s * SLOT_BYTES;
-          if (c.phase == 0) {
-            if (!mbar_test(B.q_empty, (c.t & 1) ^ 1)) continue;
-            mbar_expect_tx(B.q_full, Q_BYTES);
-            tma_load_2d(sb + SLOT_Q, &tmQ, B.q_full, c.wk.h * D, c.wk.start + c.wk.q0);
-            c.phase = 1;
-            progress = true;
-          }
-          const int b = c.g & 1;
-          if (!mbar_test(&B.kv_empty[b], ((c.g >> 1) & 1) ^ 1)) continue;
-          mbar_expect_tx(&B.kv_full[b], 2 * KV_BYTES);
-          tma_load_2d(sb + SLOT_K + b * KV_BYTES, &tmK, &B.kv_full[b], c.wk.h * D, c.wk.start + c.j * BKV);
-          tma_load_2d(sb + SLOT_V + b * KV_BYTES, &tmV, &B.kv_full[b], c.wk.h * D, c.wk.start + c.j * BKV);
-          progress = true;
-          c.g++;
-          if (++c.j == c.wk.nb) {
-            c.j = 0;
-            c.t++;
-            c.phase = 0;
-            c.w += vstride;
-            if (c.w < args.num_work) c.wk = decode(args, c.w);
-          }
-        }
-        if (!active || !wd.tick(progress, abort, args.err)) break;
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+      const int s = warp;
+      SlotBars B(bars + s * kBarsPerSlot);
+      uint8_t* sb = smem + s * SLOT_BYTES;
+      const uint32_t t_s = tmem + s * 128, t_p = t_s + 32, t_o = t_s + 64;
       const uint32_t id_s = idesc<T, BQ, BKV>();
       const uint32_t id_o = idesc<T, BQ, D, true>();
-      SlotCursor cs[kSlots];
-      uint32_t gs[kSlots];  // blocks completed by the slot (s_full / p_full phases)
-      for (int s = 0; s < kSlots; s++) {
-        cs[s] = SlotCursor{(int)blockIdx.x * kSlots + s, Work{}, 0, 0, 0, 0};
-        gs[s] = 0;
-        if (cs[s].w < args.num_work) cs[s].wk = decode(args, cs[s].w);
-      }
-      Watchdog wd{clock64(), 0};
-      for (;;) {
-        bool active = false, progress = false;
+      uint32_t gl = 0, gc = 0, gs = 0;  // K/V blocks loaded, K/V blocks consumed, S blocks
+      auto load_q = [&](const Work& wk, uint32_t t) -> bool {
+        if (!mbar_wait(B.q_empty, (t & 1) ^ 1, abort, args.err)) return false;
+        mbar_expect_tx(B.q_full, Q_BYTES);
+        tma_load_2d(sb + SLOT_Q, &tmQ, B.q_full, wk.h * D, wk.start + wk.q0);
+        return true;
+      };
+      auto load_kv = [&](const Work& wk, int j) -> bool {
+        const int b = gl & 1;
+        if (!mbar_wait(&B.kv_empty[b], ((gl >> 1) & 1) ^ 1, abort, args.err)) return false;
+        mbar_expect_tx(&B.kv_full[b], 2 * KV_BYTES);
+        tma_load_2d(sb + SLOT_K + b * KV_BYTES, &tmK, &B.kv_full[b], wk.h * D, wk.start + j * BKV);
+        tma_load_2d(sb + SLOT_V + b * KV_BYTES, &tmV, &B.kv_full[b], wk.h * D, wk.start + j * BKV);
+        gl++;
+        return true;
+      };
+      auto issue_s = [&]() -> bool {  // S = Q K^T for the next block in consumption order
+        const int b = gc & 1;
+        if (!mbar_wait(&B.kv_full[b], (gc >> 1) & 1, abort, args.err)) return false;
+        tc_fence_after();
+        const uint64_t q_desc = sw128_desc(smem_u32(sb + SLOT_Q));
+        const uint64_t k_desc = sw128_desc(smem_u32(sb + SLOT_K + b * KV_BYTES));
 #pragma unroll
-        for (int s = 0; s < kSlots; s++) {
-          SlotCursor& c = cs[s];
-          if (c.w >= args.num_work) continue;
-          active = true;
-          SlotBars B(bars + s * kBarsPerSlot);
-          uint8_t* sb = smem + s * SLOT_BYTES;
-          const uint32_t t_s = tmem + s * 128, t_p = t_s + 32, t_o = t_s + 64;
-          const int b = c.g & 1;
-          if (c.phase == 0) {  // S_j = Q K_j^T
-            if (c.j == 0 && !mbar_test(B.q_full, c.t & 1)) continue;
-            if (!mbar_test(&B.kv_full[b], (c.g >> 1) & 1)) continue;
+        for (int k = 0; k < D / 16; k++) mma_f16(t_s, q_desc + 2 * k, k_desc + 2 * k, id_s, k > 0);
+        mma_commit(B.s_full);
+        return true;
+      };
+      int w = blockIdx.x * kSlots + s;
+      if (w < args.num_work) {
+        Work cur = decode(args, w);
+        int nl = 1;  // blocks of `cur` whose loads were issued
+        bool ok = load_q(cur, 0) && load_kv(cur, 0);
+        for (uint32_t t = 0; ok; t++) {
+          const int wn = w + vstride;
+          const bool has_next = wn < args.num_work;
+          Work nxt{};
+          if (has_next) nxt = decode(args, wn);
+          if (!mbar_wait(B.q_full, t & 1, abort, args.err) || !issue_s()) break;
+          if (cur.nb == 1) mma_commit(B.q_empty);  // Q free once the item's last S ran
+          if (nl < cur.nb && !(ok = load_kv(cur, nl++))) break;
+          for (int j = 0; j < cur.nb && ok; j++) {
+            if (j == cur.nb - 1 && has_next && !(ok = load_q(nxt, t + 1) && load_kv(nxt, 0))) break;
+            if (!mbar_wait(B.p_full, gs & 1, abort, args.err) ||
+                (j == 0 && !mbar_wait(B.o_free, (t & 1) ^ 1, abort, args.err))) {  // previous item's O read
+              ok = false;
+              break;
+            }
             tc_fence_after();
-            const uint64_t q_desc = sw128_desc(smem_u32(sb + SLOT_Q));
-            const uint64_t k_desc = sw128_desc(smem_u32(sb + SLOT_K + b * KV_BYTES));
-#pragma unroll
-            for (int k = 0; k < D / 16; k++) mma_f16(t_s, q_desc + 2 * k, k_desc + 2 * k, id_s, k > 0);
-            mma_commit(B.s_full);
-            if (c.j == c.wk.nb - 1) mma_commit(B.q_empty);  // Q free once the item's last S ran
-            c.phase = 1;
-            progress = true;
-          } else {  // O += P_j V_j
-            if (!mbar_test(B.p_full, gs[s] & 1)) continue;
-            if (c.j == 0 && !mbar_test(B.o_free, (c.t & 1) ^ 1)) continue;  // previous item's O read
-            tc_fence_after();
+            const int b = gc & 1;
             const uint64_t v_desc = sw128_desc_mn(smem_u32(sb + SLOT_V + b * KV_BYTES));
 #pragma unroll
             for (int k = 0; k < BKV / 16; k++)  // 16 keys per step: 8 TMEM columns of P, +2 KB in V
-              mma_f16_ts(t_o, t_p + 8 * k, v_desc + (uint64_t)k * (2048 >> 4), id_o, (c.j > 0 || k > 0) ? 1u : 0u);
+              mma_f16_ts(t_o, t_p + 8 * k, v_desc + (uint64_t)k * (2048 >> 4), id_o, (j > 0 || k > 0) ? 1u : 0u);
             mma_commit(&B.kv_empty[b]);
-            gs[s]++;
-            c.g++;
-            c.phase = 0;
-            progress = true;
-            if (++c.j == c.wk.nb) {
-              mma_commit(B.o_full);
-              c.j = 0;
-              c.t++;
-              c.w += vstride;
-              if (c.w < args.num_work) c.wk = decode(args, c.w);
+            gc++;
+            gs++;
+            if (j + 1 < cur.nb) {
+              if (!(ok = issue_s())) break;
+              if (j + 2 == cur.nb) mma_commit(B.q_empty);
+              if (nl < cur.nb && !(ok = load_kv(cur, nl++))) break;
             }
           }
+          if (!ok) break;
+          mma_commit(B.o_full);
+          if (!has_next) break;
+          w = wn;
+          cur = nxt;
+          nl = 1;
         }
-        if (!active || !wd.tick(progress, abort, args.err)) break;
       }
     }
   } else {
