@@ -260,9 +260,10 @@ static int32_t attention_common(Ctx* c, Buf* q, Buf* k, Buf* v, Buf* out, const 
     return launch_attention_f32(c, (const float*)q->ptr, (const float*)k->ptr, (const float*)v->ptr, hidden,
                                 (float*)out->ptr, hidden, (const int32_t*)dcu.p, Bn, T, nh, dh, scale, mx);
   FL_CHECK(c, dh == 64, "Attention: 16-bit attention needs head_dim 64 (got %d)", dh);
+  FL_CHECK(c, mx <= kAttnMaxLen, "Attention: 16-bit attention takes sequences up to %d rows (got %d)", kAttnMaxLen, mx);
   std::vector<int2> tiles;
   for (int s = 0; s < Bn; s++)
-    for (int q0 = 0; q0 < lens[s]; q0 += kAttnTileRows) tiles.push_back(make_int2(s, q0));
+    for (int q0 = 0; q0 < lens[s]; q0 += kAttnTileRows) tiles.push_back(attn_tile(cu[s], lens[s], q0));
   Temp dt_(c);
   if ((rc = upload(c, dt_, tiles.data(), (int64_t)tiles.size() * 8))) return rc;
   return launch_flash_attention_tc(c, dt, q->ptr, k->ptr, v->ptr, hidden, T, hidden, out->ptr, hidden,

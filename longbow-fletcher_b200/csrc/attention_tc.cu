@@ -52,6 +52,7 @@ struct AttnArgs {
   int64_t ld_out;
   float sl2;  // scale * log2(e)
   int32_t* err;
+  int st256;  // output rows 32-byte aligned: 256-bit stores
 };
 
 struct Work {
@@ -71,6 +72,12 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+// 256-bit global store (sm_100), not allocated in L1.  dst must be 32-byte aligned.
+__device__ __forceinline__ void st_global_256(void* dst, const uint32_t (&u)[8]) {
+  asm volatile("st.global.L1::no_allocate.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(u[0]),
+               "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7])
+               : "memory");
 }
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
@@ -114,9 +121,9 @@ __device__ __forceinline__ Work decode(const AttnArgs& a, int w) {
   const int2 t = a.tiles[w / a.nh];
   Work r;
   r.h = w % a.nh;
-  r.start = a.cu[t.x];
-  r.L = a.cu[t.x + 1] - r.start;
-  r.q0 = t.y;
+  r.start = t.x;
+  r.L = (int)((uint32_t)t.y >> 16);
+  r.q0 = t.y & 0xFFFF;
   r.nb = (r.L + BKV - 1) / BKV;
   return r;
 }
@@ -268,8 +275,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t t_s = tmem + ((uint32_t)(q * 32) << 16) + s * 128, t_p = t_s + 32, t_o = t_s + 64;
     const float sl2 = args.sl2;
     uint32_t gs = 0, t = 0;
-    for (int w = blockIdx.x * kSlots + s; w < args.num_work; w += vstride, ++t) {
-      const Work wk = decode(args, w);
+    int w = blockIdx.x * kSlots + s;
+    Work nxt{};
+    if (w < args.num_work) nxt = decode(args, w);
+    for (; w < args.num_work; w += vstride, ++t) {
+      const Work wk = nxt;
+      // The next item's descriptor is fetched now; its loads complete during this item.
+      if (w + vstride < args.num_work) nxt = decode(args, w + vstride);
       float m_ref = 0.f, l = 0.f;
       bool ok = true;
       for (int j = 0; j < wk.nb; j++, gs++) {
@@ -332,14 +344,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_before();
       mbar_arrive(B.o_free);
       if (wk.q0 + r < wk.L) {
-        const float inv = 1.0f / l;
+        const float inv = __frcp_rn(l);
         T* dst = reinterpret_cast<T*>(args.out) + (int64_t)(wk.start + wk.q0 + r) * args.ld_out + wk.h * D;
+        if (args.st256) {  // four 32-byte stores: one full sector per lane
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-          const float* v = &o[c * 8];
-          reinterpret_cast<uint4*>(dst)[c] =
-              make_uint4(pack2<T>(v[0] * inv, v[1] * inv), pack2<T>(v[2] * inv, v[3] * inv),
-                         pack2<T>(v[4] * inv, v[5] * inv), pack2<T>(v[6] * inv, v[7] * inv));
+          for (int c = 0; c < 4; c++) {
+            const float* v = &o[c * 16];
+            uint32_t u[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) u[k] = pack2<T>(v[2 * k] * inv, v[2 * k + 1] * inv);
+            st_global_256(reinterpret_cast<uint8_t*>(dst) + c * 32, u);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; c++) {
+            const float* v = &o[c * 8];
+            reinterpret_cast<uint4*>(dst)[c] =
+                make_uint4(pack2<T>(v[0] * inv, v[1] * inv), pack2<T>(v[2] * inv, v[3] * inv),
+                           pack2<T>(v[4] * inv, v[5] * inv), pack2<T>(v[6] * inv, v[7] * inv));
+          }
         }
       }
     }
@@ -374,7 +397,8 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void*
   if ((rc = make_tma_map_2d(c, &mk, dt, k, (uint64_t)T, (uint64_t)H, (uint64_t)ld_in, D, BKV))) return rc;
   if ((rc = make_tma_map_2d(c, &mv, dt, v, (uint64_t)T, (uint64_t)H, (uint64_t)ld_in, D, BKV))) return rc;
   const int work = num_tiles * nh;
-  AttnArgs a{cu, tiles128, work, nh, out, ld_out, scale * 1.4426950408889634f, c->d_err};
+  const int st256 = ((uintptr_t)out & 31) == 0 && (ld_out * 2) % 32 == 0;
+  AttnArgs a{cu, tiles128, work, nh, out, ld_out, scale * 1.4426950408889634f, c->d_err, st256};
   static bool attr_set[2][64] = {};
   const int ti = dt == FLETCHER_BF16 ? 0 : 1;
   if (!attr_set[ti][c->device & 63]) {

@@ -53,13 +53,19 @@ int32_t launch_attention_f32(Ctx* c, const float* q, const float* k, const float
                              int64_t T, int32_t nh, int32_t dh, float scale, int32_t max_len);
 
 // bf16/f16 flash attention on tcgen05 (attention_tc.cu), head_dim 64: q/k/v [T, H] views with
-// row stride ld_in; tiles128: int2 {seq, q_row_start} per 128-row query tile.
+// row stride ld_in; tiles128: one attn_tile() per 128-row query tile.
 int32_t launch_flash_attention_tc(Ctx* c, int32_t dtype, const void* q, const void* k, const void* v,
                                   int64_t ld_in, int64_t T, int64_t H, void* out, int64_t ld_out,
                                   const int32_t* cu_seqlens, const int2* tiles128, int32_t num_tiles,
                                   int32_t nh, float scale);
-// Query-tile height of launch_flash_attention_tc.
+// Query-tile height of launch_flash_attention_tc, and the longest sequence it takes.
 constexpr int kAttnTileRows = 128;
+constexpr int kAttnMaxLen = 65535;
+// Query-tile descriptor: {first row of the sequence, (sequence length << 16) | first query row
+// of the tile within the sequence}; self-contained, so the kernel decodes it with one load.
+inline int2 attn_tile(int32_t seq_start, int32_t len, int32_t q0) {
+  return make_int2(seq_start, (int32_t)(((uint32_t)len << 16) | (uint32_t)q0));
+}
 
 // Elementwise helpers.
 int32_t launch_scale_add(Ctx* c, int32_t dtype, void* x, const void* other, float scale,

@@ -310,6 +310,7 @@ static int32_t upload_meta(Model* m, const int32_t* lengths, int32_t B, int64_t 
     mx = std::max(mx, lengths[i]);
   }
   FL_CHECK(c, nt <= m->tiles_cap, "internal: tile list overflow");
+  FL_CHECK(c, mx <= kAttnMaxLen, "ForwardBatch: sequences are limited to %d tokens (got %d)", kAttnMaxLen, mx);
   const int64_t bytes = (int64_t)(B + 1) * 4 + nt * 8 + 16;
   if (bytes > m->h_meta_cap) {
     if (m->h_meta) {
@@ -330,7 +331,7 @@ static int32_t upload_meta(Model* m, const int32_t* lengths, int32_t B, int64_t 
   int64_t k = 0;
   for (int oi = 0; oi < B; oi++) {
     const int s = order[oi];
-    for (int q0 = 0; q0 < lengths[s]; q0 += kAttnTileRows) tl[k++] = make_int2(s, q0);
+    for (int q0 = 0; q0 < lengths[s]; q0 += kAttnTileRows) tl[k++] = attn_tile(cu[s], lengths[s], q0);
   }
   FL_CUDA(c, cudaMemcpyAsync(m->d_cu, cu, (B + 1) * 4, cudaMemcpyHostToDevice, c->stream));
   if (nt) FL_CUDA(c, cudaMemcpyAsync(m->d_tiles, tl, nt * 8, cudaMemcpyHostToDevice, c->stream));

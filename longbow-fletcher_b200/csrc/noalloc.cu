@@ -80,6 +80,8 @@ extern "C" int32_t Cuda_Attention_VarLen_NoAlloc(CudaContextRef ctx, CudaBufferR
     tiles += (lengths[i] + kAttnTileRows - 1) / kAttnTileRows;
     mx = lengths[i] > mx ? lengths[i] : mx;
   }
+  FL_CHECK(c, dt == FLETCHER_F32 || mx <= kAttnMaxLen,
+           "AttentionVarLen_NoAlloc: 16-bit attention takes sequences up to %d rows (got %d)", kAttnMaxLen, mx);
   const int64_t es = dtype_size(dt);
   FL_CHECK(c, T * hidden * es <= q->bytes && T * hidden * es <= k->bytes && T * hidden * es <= v->bytes &&
                   T * hidden * es <= o->bytes,
@@ -101,8 +103,9 @@ extern "C" int32_t Cuda_Attention_VarLen_NoAlloc(CudaContextRef ctx, CudaBufferR
     int64_t t = tiles_off;
     for (int s = 0; s < numSeqs; s++)
       for (int q0 = 0; q0 < lengths[s]; q0 += kAttnTileRows) {
-        g_host[t++] = s;
-        g_host[t++] = q0;
+        const int2 d = attn_tile(g_host[s], lengths[s], q0);
+        g_host[t++] = d.x;
+        g_host[t++] = d.y;
       }
   }
   FL_CUDA(c, cudaMemcpyAsync(dscr, g_host, need * 4, cudaMemcpyHostToDevice, c->stream));
