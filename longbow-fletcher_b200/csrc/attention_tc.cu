@@ -17,9 +17,9 @@
 //   warps 2-5 : softmax of slot 0, warps 6-9 softmax of slot 1 — thread = query row: tcgen05.ld
 //               its S row, mask keys past the sequence end, exp2 against a lazily updated
 //               reference max, and tcgen05.st P (16-bit pairs) over the upper half of S.  The
-//               reference max moves only when a row's block max exceeds it by more than 2^8 in
-//               exp2 terms; then O (complete, because S_j's commit follows PV_{j-1}) is rescaled
-//               in TMEM.  At the end of an item the row of O is divided by its sum and stored.
+//               reference max starts at the row's first key and moves only when some P exceeds
+//               2^64 (bf16; 2^15 for fp16), found from the block's largest P after the exps; then
+//               O (complete, because S_j's commit follows PV_{j-1}) is rescaled in TMEM.  At the end of an item the row of O is divided by its sum and stored.
 // TMEM per slot: S/P 64 columns + O 64 columns; 256 per CTA.  ~98 KB smem.  All mbarrier waits
 // are bounded (device error flag + abort, as in the GEMM).  No multicast.
 #include "tc_common.cuh"
@@ -41,7 +41,6 @@ constexpr int kBarsPerSlot = 10;
 constexpr int OFF_BAR = kSlots * SLOT_BYTES;
 constexpr int SMEM = OFF_BAR + kSlots * kBarsPerSlot * 8 + 16 + 1024;
 constexpr int TMEM_COLS = 256;  // slot s: S [128s, 128s+64) with P in its upper 32 columns, O [128s+64, 128s+128)
-constexpr float kRescaleLog2 = 8.0f;  // P <= 2^8 between reference-max updates
 
 struct AttnArgs {
   const int32_t* cu;
@@ -115,6 +114,32 @@ __device__ __forceinline__ float row_max(const float (&sv)[BKV]) {
 #pragma unroll
   for (int k = 0; k < 8; k++) mp[k] = fmaxf(mp[k], sv[56 + k]);
   return max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+}
+
+// Largest P between reference-max updates: 2^64 for bf16 (fp32 O and row sums stay far from
+// overflow), 2^15 for fp16 (its largest finite value is 65504).
+template <typename T>
+__device__ __forceinline__ float kPMax() {
+  return std::is_same<T, __nv_bfloat16>::value ? 18446744073709551616.0f : 32768.0f;
+}
+
+// P = 2^(S * scale * log2 e - ms) for a 64-key row: 16-bit pairs in pk, fp32 sum in `sum`;
+// returns the largest P.
+template <typename T>
+__device__ __forceinline__ float exp_row(float (&sv)[BKV], float sl2, float ms, uint32_t (&pk)[32], float& sum) {
+  float ra[4][2] = {};  // four independent packed partial sums
+  float pm[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < BKV; i += 2) {
+    fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
+    sv[i] = ex2(sv[i]);
+    sv[i + 1] = ex2(sv[i + 1]);
+    add2(ra[(i >> 1) & 3][0], ra[(i >> 1) & 3][1], sv[i], sv[i + 1]);
+    pm[(i >> 1) & 3] = max3(pm[(i >> 1) & 3], sv[i], sv[i + 1]);
+    pk[i >> 1] = pack2<T>(sv[i], sv[i + 1]);
+  }
+  sum = ((ra[0][0] + ra[0][1]) + (ra[1][0] + ra[1][1])) + ((ra[2][0] + ra[2][1]) + (ra[3][0] + ra[3][1]));
+  return fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
 }
 
 __device__ __forceinline__ Work decode(const AttnArgs& a, int w) {
@@ -294,19 +319,28 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_ld64(t_s, sv);
         const int valid = wk.L - j * BKV;  // keys of this block inside the sequence (>= 1)
         if (valid < BKV) mask_tail(sv, valid);
-        const float mx = row_max(sv);
-        if (j == 0) {
-          m_ref = mx;
-        } else {
-          const bool need = (mx - m_ref) * sl2 > kRescaleLog2;
-          if (__any_sync(0xffffffffu, need)) {
-            // Rare path.  O holds PV_0..PV_{j-1} complete (S_j's commit came after PV_{j-1});
-            // the S row is reloaded afterwards so that it is not live across the rescale.
-            const float f = need ? ex2((m_ref - mx) * sl2) : 1.0f;
-            if (need) {
-              m_ref = mx;
-              l *= f;
-            }
+        // P against the current reference max (for block 0: the row's first key, which is never
+        // above the row max, so the dominant terms cannot underflow); the block max is checked
+        // afterwards through the largest P.
+        if (j == 0) m_ref = sv[0];
+        float rsum;
+        uint32_t pk[32];
+        const float pmax = exp_row<T>(sv, sl2, m_ref * sl2, pk, rsum);
+        const bool need = !(pmax <= kPMax<T>());
+        if (__any_sync(0xffffffffu, need)) {
+          // Rare path: some row's max moved by more than the P range allows.  S is still in
+          // TMEM (P is not written yet); O holds PV_0..PV_{j-1} complete (S_j's commit came
+          // after PV_{j-1}).
+          tmem_ld64(t_s, sv);
+          if (valid < BKV) mask_tail(sv, valid);
+          const float mx = row_max(sv);
+          float f = 1.0f;
+          if (need) {
+            f = ex2((m_ref - mx) * sl2);
+            m_ref = mx;
+            l *= f;
+          }
+          if (j > 0) {
 #pragma unroll 1
             for (int hh = 0; hh < 2; hh++) {
               float ov[32];
@@ -316,26 +350,16 @@ __global__ void __launch_bounds__(kThreads, 2)
               for (int c = 0; c < 32; c++) ou[c] = __float_as_uint(ov[c] * f);
               tmem_st32(t_o + hh * 32, ou);
             }
-            tmem_ld64(t_s, sv);
-            if (valid < BKV) mask_tail(sv, valid);
           }
-        }
-        const float ms = m_ref * sl2;
-        float ra[4][2] = {};  // four independent packed partial sums
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < BKV; i += 2) {
-          fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
-          sv[i] = ex2(sv[i]);
-          sv[i + 1] = ex2(sv[i + 1]);
-          add2(ra[(i >> 1) & 3][0], ra[(i >> 1) & 3][1], sv[i], sv[i + 1]);
-          pk[i >> 1] = pack2<T>(sv[i], sv[i + 1]);
+          tmem_ld64(t_s, sv);
+          if (valid < BKV) mask_tail(sv, valid);
+          exp_row<T>(sv, sl2, m_ref * sl2, pk, rsum);
         }
         tmem_st32(t_p, pk);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(B.p_full);
-        l += ((ra[0][0] + ra[0][1]) + (ra[1][0] + ra[1][1])) + ((ra[2][0] + ra[2][1]) + (ra[3][0] + ra[3][1]));
+        l += rsum;
       }
       if (!ok || !mbar_wait(B.o_full, t & 1, abort, args.err)) break;
       tc_fence_after();

@@ -138,6 +138,28 @@ def test_flash_attention_varlen(fl, be, lengths, dtype):
     assert np.abs(got - want).max() < (3e-2 if dtype == "bf16" else 5e-3)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_flash_attention_moving_max(fl, be, dtype):
+    """Scores spread over hundreds of units: row maxima jump between 64-key blocks by more than
+    the P range (2^64 for bf16, 2^15 for fp16), so the kernel's reference-max update and O
+    rescale run, including on rows whose first key is far below the row max."""
+    rng = np.random.default_rng(11)
+    lengths = [700, 130, 64, 1, 257]
+    H, nh = 768, 12
+    T = sum(lengths)
+    q = (rng.standard_normal((T, H)) * 6).astype(np.float32)
+    k = (rng.standard_normal((T, H)) * 6).astype(np.float32)
+    v = rng.standard_normal((T, H)).astype(np.float32)
+    k[650] *= 4  # a late key with much larger scores in the first sequence
+    dt = fl.DTYPES[dtype]
+    tq, tk, tv = (be.new_tensor(T, H, a, dt) for a in (q, k, v))
+    got = tq.attention_varlen(tq, tk, tv, lengths, nh, 0.125).to_host()
+    qq = bf16_round if dtype == "bf16" else (lambda a: a.astype(np.float16).astype(np.float32))
+    want = attention_np(qq(q), qq(k), qq(v), lengths, nh, 0.125, fast=False)
+    assert np.isfinite(got).all()
+    assert np.abs(got - want).max() < (6e-2 if dtype == "bf16" else 2e-2)
+
+
 def test_attention_uniform_matches_varlen(fl, be):
     rng = np.random.default_rng(0)
     B, S, H, nh = 3, 40, 128, 2
