@@ -24,6 +24,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -38,11 +39,17 @@ constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;            // + producer warp + MMA warp
 constexpr int kStageOut = 32 * 128;                    // per-warp output box: 32 rows x 64 cols x 2 B
 
-template <int BN>
+// PAIR: the tile is computed by a cluster of two CTAs on two SMs with tcgen05 cta_group::2
+// (M = 256 per MMA): each CTA loads its 128 rows of A and half of the tile's BN rows of W, and
+// holds its 128 rows of the accumulator.  Per SM that is a third less operand traffic than a
+// 128 x 256 tile on one SM.
+template <int BN, bool PAIR>
 struct Cfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of W loaded by one CTA
+  static constexpr int TILE_M = PAIR ? 2 * BM : BM;  // rows of a tile
+  static constexpr int STAGES = (BM + B_ROWS) * BK * 2 <= 32768 ? ((BM + B_ROWS) * BK * 2 <= 24576 ? 8 : 6) : 4;
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int OUT_OFF = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = OUT_OFF + kEpiWarps * kStageOut;
@@ -88,11 +95,11 @@ __device__ __forceinline__ void load32(const T* src, float (&v)[32]) {
   }
 }
 
-template <typename T, int BN, int EPI>
+template <typename T, int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -110,6 +117,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = args.num_n_tiles;
   const int num_tiles = args.num_m_tiles * n_tiles;
   const int num_kb = args.K / BK;
+  // Pair mode: clusters of two consecutive CTAs; CTA rank 0 issues the MMAs.
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0;
+  const int first_tile = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tile_stride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; i++) {
@@ -118,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], kEpiThreads);
+      mbar_init(&tempty[i], PAIR ? 2 * kEpiWarps : kEpiWarps);  // one arrival per epilogue warp (of both CTAs)
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -129,13 +140,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmC) : "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
-                 "r"(C::TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                   "r"(C::TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                   "r"(C::TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -143,13 +164,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
         const int mb = tile / n_tiles, nb = tile % n_tiles;
+        const int a_row = mb * C::TILE_M + (int)crank * BM;
+        const int b_row = nb * BN + (int)crank * C::B_ROWS;
         for (int kb = 0; kb < num_kb; kb++) {
           if (!mbar_wait_spin(&empty[stage], phase ^ 1, abort, args.err)) goto producer_done;
-          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, mb * BM);
-          tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+          if constexpr (PAIR) {
+            // Both CTAs' loads complete on the even CTA's barrier, which expects both.
+            if (crank == 0) mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, fb, kb * BK, a_row);
+            tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, fb, kb * BK, b_row);
+          } else {
+            mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+            tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, a_row);
+            tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, b_row);
+          }
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
@@ -159,12 +190,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     producer_done:;
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t id = idesc<T, BM, BN>();
+    if (lane == 0 && crank == 0) {
+      const uint32_t id = idesc<T, C::TILE_M, BN>();
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      for (int tile = first_tile; tile < num_tiles; tile += tile_stride, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait_spin(&tempty[acc], acc_phase ^ 1, abort, args.err)) break;
@@ -180,16 +211,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t a_desc = sw128_desc(smem_u32(sA + stage * C::A_BYTES));
           const uint64_t b_desc = sw128_desc(smem_u32(sB + stage * C::B_BYTES));
 #pragma unroll
-          for (int k = 0; k < BK / 16; k++)  // +32 bytes per K=16 step inside the swizzle atom
-            mma_f16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, id, (kb | k) != 0);
-          mma_commit(&empty[stage]);
+          for (int k = 0; k < BK / 16; k++) {  // +32 bytes per K=16 step inside the swizzle atom
+            if constexpr (PAIR)
+              mma_f16_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, id, (kb | k) != 0);
+            else
+              mma_f16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, id, (kb | k) != 0);
+          }
+          if constexpr (PAIR)
+            mma_commit_pair(&empty[stage]);  // frees the stage in both CTAs
+          else
+            mma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        mma_commit(&tfull[acc]);
+        if constexpr (PAIR)
+          mma_commit_pair(&tfull[acc]);
+        else
+          mma_commit(&tfull[acc]);
       }
     }
   } else {
@@ -201,13 +242,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int UNITS = EPI == EPI_SWIGLU ? BN / 256 : BN / 128;
     const int64_t n_out = EPI == EPI_SWIGLU ? args.N / 2 : args.N;
     int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+    const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0;
+    for (int tile = first_tile; tile < num_tiles; tile += tile_stride, ++it) {
       const int mb = tile / n_tiles, nb = tile % n_tiles;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_spin(&tfull[acc], acc_phase, abort, args.err)) break;
       tc_fence_after();
-      const int row0 = mb * BM + q * 32;
+      const int row0 = mb * C::TILE_M + (int)crank * BM + q * 32;
       const int64_t row = (int64_t)row0 + lane;
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
@@ -307,7 +349,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (u == UNITS - 1) {  // every TMEM read of this tile is done: release the accumulator
           tc_fence_before();
-          mbar_arrive(&tempty[acc]);
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (PAIR)
+              mbar_arrive_cluster(tempty_lead + acc * 8);  // the even CTA's MMA waits for both CTAs
+            else
+              mbar_arrive(&tempty[acc]);
+          }
         }
         if (ocol < n_out && row0 < args.M) {
           if (lane == 0) bulk_wait_read0();  // the previous box has left the staging buffer
@@ -326,11 +374,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // no cross-CTA signal or MMA is in flight past this point
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
-                 : "memory");
+    if constexpr (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
+                   : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
+                   : "memory");
   }
 }
 
@@ -365,36 +420,54 @@ static int32_t make_map(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, 
   return FLETCHER_OK;
 }
 
-template <typename T, int BN, int EPI>
+template <typename T, int BN, int EPI, bool PAIR>
 static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmArgs a) {
-  using Cf = Cfg<BN>;
+  using Cf = Cfg<BN, PAIR>;
+  auto kern = k_gemm_tc<T, BN, EPI, PAIR>;
   static bool attr_set[64] = {};  // per device
   if (!attr_set[c->device & 63]) {
-    FL_CUDA(c, cudaFuncSetAttribute(k_gemm_tc<T, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
+    FL_CUDA(c, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
     attr_set[c->device & 63] = true;
   }
-  a.num_m_tiles = (int)((a.M + BM - 1) / BM);
+  a.num_m_tiles = (int)((a.M + Cf::TILE_M - 1) / Cf::TILE_M);
   a.num_n_tiles = (int)((a.N + BN - 1) / BN);
   const int tiles = a.num_m_tiles * a.num_n_tiles;
-  const int grid = tiles < c->num_sms ? tiles : c->num_sms;
-  k_gemm_tc<T, BN, EPI><<<grid, kThreads, Cf::SMEM, c->stream>>>(ma, mb, mc, a);
+  if constexpr (PAIR) {
+    const int pairs = c->num_sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (tiles < pairs ? tiles : pairs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cf::SMEM;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    FL_CUDA(c, cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, a));
+  } else {
+    const int grid = tiles < c->num_sms ? tiles : c->num_sms;
+    kern<<<grid, kThreads, Cf::SMEM, c->stream>>>(ma, mb, mc, a);
+  }
   FL_LAUNCH(c);
   return FLETCHER_OK;
 }
 
-template <typename T>
+template <typename T, bool PAIR>
 static int32_t dispatch(Ctx* c, int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
                         const GemmArgs& a) {
-#define FL_EPI(E)                                                                \
-  case E:                                                                        \
-    return bn == 256 ? run<T, 256, E>(c, ma, mb, mc, a) : run<T, 128, E>(c, ma, mb, mc, a);
+#define FL_EPI(E)                                                                            \
+  case E:                                                                                    \
+    return bn == 256 ? run<T, 256, E, PAIR>(c, ma, mb, mc, a) : run<T, 128, E, PAIR>(c, ma, mb, mc, a);
   switch (epi) {
     FL_EPI(EPI_STORE)
     FL_EPI(EPI_ROPE)
     FL_EPI(EPI_GELU)
     FL_EPI(EPI_RESIDUAL)
     case EPI_SWIGLU:
-      return run<T, 256, EPI_SWIGLU>(c, ma, mb, mc, a);
+      return run<T, 256, EPI_SWIGLU, PAIR>(c, ma, mb, mc, a);
   }
 #undef FL_EPI
   return set_error(c, FLETCHER_ERR_INVALID, "gemm: unknown epilogue %d", epi);
@@ -405,6 +478,15 @@ static int32_t dispatch(Ctx* c, int epi, int bn, const CUtensorMap& ma, const CU
 int32_t make_tma_map_2d(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, uint64_t rows, uint64_t cols,
                         uint64_t ld, uint32_t box_cols, uint32_t box_rows) {
   return tc::make_map(c, m, dtype, ptr, rows, cols, ld, box_cols, box_rows);
+}
+
+// FLETCHER_GEMM_PAIR=0 selects single-SM tiles everywhere (for A/B measurement).
+bool gemm_pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("FLETCHER_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 bool gemm_tc_supported(int64_t M, int64_t N, int64_t K, int bn) {
@@ -423,10 +505,12 @@ int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, in
   FL_CHECK(c, epi != EPI_RESIDUAL || (((uintptr_t)residual & 15) == 0 && ld_res % 8 == 0),
            "gemm_tc: residual must be 16-byte aligned");
   const int64_t n_out = epi == EPI_SWIGLU ? N / 2 : N;
+  // CTA pairs (2-SM MMAs) once there are enough 256-row tiles to fill the GPU.
+  const bool pair = gemm_pair_enabled() && M >= 2048;
   CUtensorMap ma, mb, mc;
   int32_t rc = tc::make_map(c, &ma, dtype, A, (uint64_t)M, (uint64_t)K, (uint64_t)K, tc::BK, tc::BM);
   if (rc) return rc;
-  rc = tc::make_map(c, &mb, dtype, W, (uint64_t)N, (uint64_t)K, (uint64_t)K, tc::BK, (uint32_t)bn);
+  rc = tc::make_map(c, &mb, dtype, W, (uint64_t)N, (uint64_t)K, (uint64_t)K, tc::BK, (uint32_t)(pair ? bn / 2 : bn));
   if (rc) return rc;
   rc = tc::make_map(c, &mc, dtype, out, (uint64_t)M, (uint64_t)n_out, (uint64_t)ld_out, 64, 32);
   if (rc) return rc;
@@ -444,8 +528,12 @@ int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, in
   a.sin_t = sin_t;
   a.rope_cols = rope_cols;
   a.err = c->d_err;
-  if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16>(c, epi, bn, ma, mb, mc, a);
-  return tc::dispatch<__half>(c, epi, bn, ma, mb, mc, a);
+  if (pair) {
+    if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16, true>(c, epi, bn, ma, mb, mc, a);
+    return tc::dispatch<__half, true>(c, epi, bn, ma, mb, mc, a);
+  }
+  if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16, false>(c, epi, bn, ma, mb, mc, a);
+  return tc::dispatch<__half, false>(c, epi, bn, ma, mb, mc, a);
 }
 
 }  // namespace fl
