@@ -12,8 +12,10 @@
 //   warp 0   : TMA producer — one thread streams A/W slabs into a STAGES-deep smem ring;
 //   warp 1   : MMA issuer — one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two
 //              TMEM accumulators and commits to mbarriers; the warp also owns TMEM alloc;
-//   warps 2-9: epilogue — warp w reads TMEM lane quarter w%4 with tcgen05.ld (warps 2-5 take
-//              the first half of the tile's columns, warps 6-9 the second half), applies bias /
+//   warps 2-9: epilogue — for store / RoPE / GELU two groups of four warps take alternate
+//              tiles (accumulator 0 / 1), for residual / SwiGLU warps 2-5 and 6-9 take the
+//              two column halves of every tile; warp w reads TMEM lane quarter w%4 with
+//              tcgen05.ld, applies bias /
 //              RoPE / GELU / SwiGLU / residual in registers, writes 32x64 output boxes into a
 //              per-warp 128B-swizzled smem buffer and stores them with TMA bulk-tensor stores
 //              (full-line, asynchronous writes instead of per-thread 16-byte row stores).
@@ -38,6 +40,10 @@ constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;            // + producer warp + MMA warp
 constexpr int kStageOut = 32 * 128;                    // per-warp output box: 32 rows x 64 cols x 2 B
+constexpr int kOutBufs = 2;                            // output boxes in flight per warp
+// Epilogues drained by alternating warp groups (see the epilogue section of k_gemm_tc).
+template <int EPI>
+constexpr bool kEpiGroups = EPI == 0 || EPI == 1 || EPI == 2;  // EPI_STORE, EPI_ROPE, EPI_GELU
 
 // PAIR: the tile is computed by a cluster of two CTAs on two SMs with tcgen05 cta_group::2
 // (M = 256 per MMA): each CTA loads its 128 rows of A and half of the tile's BN rows of W, and
@@ -47,12 +53,15 @@ template <int BN, bool PAIR>
 struct Cfg {
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of W loaded by one CTA
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;  // rows of a tile
-  static constexpr int STAGES = (BM + B_ROWS) * BK * 2 <= 32768 ? ((BM + B_ROWS) * BK * 2 <= 24576 ? 8 : 6) : 4;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int OUT_BYTES = kEpiWarps * kOutBufs * kStageOut;
+  // As many operand stages as fit next to the output staging (at most 8).
+  static constexpr int STAGES_FIT = (232448 - 1024 - 256 - OUT_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT < 8 ? STAGES_FIT : 8;
   static constexpr int OUT_OFF = STAGES * STAGE_BYTES;
-  static constexpr int BAR_OFF = OUT_OFF + kEpiWarps * kStageOut;
+  static constexpr int BAR_OFF = OUT_OFF + OUT_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM = BAR_OFF + 256 /*barriers*/ + 1024 /*alignment slack*/;
   static_assert(SMEM <= 232448, "shared memory budget");
@@ -73,23 +82,23 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int r, const float (&a)[
   }
 }
 
+// v[i] += the 32 16-bit values in q[0..3].
 template <typename T>
-__device__ __forceinline__ void load32(const T* src, float (&v)[32]) {
-  const uint4* s = reinterpret_cast<const uint4*>(src);
+__device__ __forceinline__ void add_packed(float (&v)[32], const uint4* q4) {
 #pragma unroll
   for (int i = 0; i < 4; i++) {
-    uint4 q = s[i];
+    const uint4 q = q4[i];
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       if constexpr (std::is_same<T, __nv_bfloat16>::value) {
         float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
-        v[8 * i + 2 * j] = f.x;
-        v[8 * i + 2 * j + 1] = f.y;
+        v[8 * i + 2 * j] += f.x;
+        v[8 * i + 2 * j + 1] += f.y;
       } else {
         float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
-        v[8 * i + 2 * j] = f.x;
-        v[8 * i + 2 * j + 1] = f.y;
+        v[8 * i + 2 * j] += f.x;
+        v[8 * i + 2 * j + 1] += f.y;
       }
     }
   }
@@ -129,7 +138,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], PAIR ? 2 * kEpiWarps : kEpiWarps);  // one arrival per epilogue warp (of both CTAs)
+      // One arrival per draining warp (of both CTAs).
+      mbar_init(&tempty[i], (kEpiGroups<EPI> ? kEpiWarps / 2 : kEpiWarps) * (PAIR ? 2 : 1));
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -235,30 +245,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // Epilogue.  Warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32): rows q*32.. of the tile.
+    // GROUPS (store / RoPE / GELU): two groups of four warps take alternate tiles (group g
+    // always drains accumulator g), so each group has two tiles' worth of MMA time for its tile
+    // and one group's RoPE-table latency overlaps the other's work.  Otherwise (residual,
+    // SwiGLU, whose per-unit loads or math want fewer units per warp) all eight warps drain
+    // every tile, warps 2-5 the first half of its columns and warps 6-9 the second.
+    constexpr bool GROUPS = kEpiGroups<EPI>;
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;  // which half of the tile's columns
-    uint8_t* stg = smem + C::OUT_OFF + (warp - 2) * kStageOut;
+    const int grp = GROUPS ? (warp - 2) >> 2 : 0;
+    const int col0 = GROUPS ? 0 : ((warp - 2) >> 2) * (EPI == EPI_SWIGLU ? 64 : BN / 2);
+    uint8_t* stg0 = smem + C::OUT_OFF + (warp - 2) * kOutBufs * kStageOut;
+    int ob = 0;  // output buffer of the next box
     // 64-column output units per warp: SwiGLU halves the width (BN/2 outputs per tile).
-    constexpr int UNITS = EPI == EPI_SWIGLU ? BN / 256 : BN / 128;
+    constexpr int UNITS = (EPI == EPI_SWIGLU ? BN / 128 : BN / 64) / (GROUPS ? 1 : 2);
+    const int tstep = GROUPS ? 2 : 1;
     const int64_t n_out = EPI == EPI_SWIGLU ? args.N / 2 : args.N;
-    int it = 0;
+    int it = grp;
     const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0;
-    for (int tile = first_tile; tile < num_tiles; tile += tile_stride, ++it) {
+    auto tile_row = [&](int t) -> int64_t {
+      return (int64_t)(t / n_tiles) * C::TILE_M + (int)crank * BM + q * 32 + lane;
+    };
+    // RoPE positions run one tile ahead, so a tile's table loads need no dependent load.
+    const int t0 = first_tile + grp * tile_stride;
+    int pos_next = 0;
+    if constexpr (EPI == EPI_ROPE) {
+      if (t0 < num_tiles && tile_row(t0) < args.M) pos_next = args.pos[tile_row(t0)];
+    }
+    for (int tile = t0; tile < num_tiles; tile += tstep * tile_stride, it += tstep) {
       const int mb = tile / n_tiles, nb = tile % n_tiles;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait_spin(&tfull[acc], acc_phase, abort, args.err)) break;
-      tc_fence_after();
       const int row0 = mb * C::TILE_M + (int)crank * BM + q * 32;
       const int64_t row = (int64_t)row0 + lane;
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       // RoPE: every 64-wide head of this row uses the same cos/sin (same position, same
-      // frequencies), so the row's table entries are loaded once per tile, not once per head.
+      // frequencies), so the row's table entries are loaded once per tile, not once per head;
+      // they are requested before the wait for the accumulator.
       float rc[EPI == EPI_ROPE ? 32 : 1], rs[EPI == EPI_ROPE ? 32 : 1];
       if constexpr (EPI == EPI_ROPE) {
+        const int p = pos_next;
+        const int nt = tile + tstep * tile_stride;
+        if (nt < num_tiles && tile_row(nt) < args.M) pos_next = args.pos[tile_row(nt)];
         if (row_ok && (int64_t)nb * BN < args.rope_cols) {
-          const int p = args.pos[row];
           const float4* ct = reinterpret_cast<const float4*>(args.cos_t + (int64_t)p * 32);
           const float4* st = reinterpret_cast<const float4*>(args.sin_t + (int64_t)p * 32);
 #pragma unroll
@@ -269,17 +298,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      // Residual: each unit's 128 bytes of the row are requested before its accumulator load
+      // (the first unit's before the wait for the accumulator).
+      uint4 res[EPI == EPI_RESIDUAL ? 8 : 1];
+      auto load_res = [&](int u) {
+        if constexpr (EPI == EPI_RESIDUAL) {
+          const int64_t oc = (int64_t)nb * BN + col0 + u * 64;
+          if (row_ok && oc < args.N) {
+            const uint4* rp =
+                reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(args.residual) + row * args.ld_res + oc);
+#pragma unroll
+            for (int i = 0; i < 8; i++) res[i] = rp[i];
+          }
+        }
+      };
+      load_res(0);
+      if (!mbar_wait_spin(&tfull[acc], acc_phase, abort, args.err)) break;
+      tc_fence_after();
 #pragma unroll 1
       for (int u = 0; u < UNITS; u++) {
         float a[32], b[32];
         int64_t ocol;
         if constexpr (EPI == EPI_SWIGLU) {
           // Tile columns [0, BN/2) hold gate rows, [BN/2, BN) the matching up rows; this unit
-          // produces output columns [half*64, half*64+64) of the tile's BN/2.
-          const int g0 = half * 64 + u * 64;  // gate column within the tile
+          // produces output columns [col0 + u*64, col0 + u*64 + 64) of the tile's BN/2.
+          const int g0 = col0 + u * 64;  // gate column within the tile
           float g[32], v[32];
-          tmem_ld32(tbase + g0, g);
-          tmem_ld32(tbase + BN / 2 + g0, v);
+          tmem_ld32x2(tbase + g0, tbase + BN / 2 + g0, g, v);
           const int pcol = nb * BN + g0;
           if (args.bias) {
 #pragma unroll
@@ -290,8 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
 #pragma unroll
           for (int i = 0; i < 32; i++) a[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * v[i];
-          tmem_ld32(tbase + g0 + 32, g);
-          tmem_ld32(tbase + BN / 2 + g0 + 32, v);
+          tmem_ld32x2(tbase + g0 + 32, tbase + BN / 2 + g0 + 32, g, v);
           if (args.bias) {
 #pragma unroll
             for (int i = 0; i < 32; i++) {
@@ -303,10 +347,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; i++) b[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * v[i];
           ocol = (int64_t)nb * (BN / 2) + g0;
         } else {
-          const int c0 = half * (BN / 2) + u * 64;  // first column of the unit within the tile
-          tmem_ld32(tbase + c0, a);
-          tmem_ld32(tbase + c0 + 32, b);
+          const int c0 = col0 + u * 64;  // first column of the unit within the tile
           ocol = (int64_t)nb * BN + c0;
+          if (u > 0) load_res(u);
+          tmem_ld32x2(tbase + c0, a, b);
           if (ocol < args.N) {
             if (args.bias) {
 #pragma unroll
@@ -335,14 +379,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if constexpr (EPI == EPI_RESIDUAL) {
               if (row_ok) {
-                float r[32];
-                const T* rp = reinterpret_cast<const T*>(args.residual) + row * args.ld_res + ocol;
-                load32<T>(rp, r);
-#pragma unroll
-                for (int i = 0; i < 32; i++) a[i] += r[i];
-                load32<T>(rp + 32, r);
-#pragma unroll
-                for (int i = 0; i < 32; i++) b[i] += r[i];
+                add_packed<T>(a, res);
+                add_packed<T>(b, res + 4);
               }
             }
           }
@@ -358,7 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (ocol < n_out && row0 < args.M) {
-          if (lane == 0) bulk_wait_read0();  // the previous box has left the staging buffer
+          uint8_t* stg = stg0 + ob * kStageOut;
+          if (lane == 0) bulk_wait_read1();  // the box stored from this buffer has left it
           __syncwarp();
           stage_row<T>(stg, lane, a, b);
           fence_async_smem();
@@ -367,6 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_store_2d(&tmC, stg, (int)ocol, row0);  // rows >= M are clipped by TMA
             bulk_commit();
           }
+          ob ^= 1;
         }
       }
     }

@@ -130,6 +130,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -182,6 +183,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
+
+// Two 32-column loads (any columns of this thread's lane) completed by one wait.
+#define FL_TMEM_LD32_ASM(ADDR, R)                                                                                    \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"        \
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                            \
+               : "=r"(R[0]), "=r"(R[1]), "=r"(R[2]), "=r"(R[3]), "=r"(R[4]), "=r"(R[5]), "=r"(R[6]), "=r"(R[7]),      \
+                 "=r"(R[8]), "=r"(R[9]), "=r"(R[10]), "=r"(R[11]), "=r"(R[12]), "=r"(R[13]), "=r"(R[14]),              \
+                 "=r"(R[15]), "=r"(R[16]), "=r"(R[17]), "=r"(R[18]), "=r"(R[19]), "=r"(R[20]), "=r"(R[21]),            \
+                 "=r"(R[22]), "=r"(R[23]), "=r"(R[24]), "=r"(R[25]), "=r"(R[26]), "=r"(R[27]), "=r"(R[28]),            \
+                 "=r"(R[29]), "=r"(R[30]), "=r"(R[31])                                                                \
+               : "r"(ADDR))
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, float (&a)[32], float (&b)[32]) {
+  uint32_t ra[32], rb[32];
+  FL_TMEM_LD32_ASM(ta, ra);
+  FL_TMEM_LD32_ASM(tb, rb);
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) {
+    a[i] = __uint_as_float(ra[i]);
+    b[i] = __uint_as_float(rb[i]);
+  }
+}
+__device__ __forceinline__ void tmem_ld32x2(uint32_t t, float (&a)[32], float (&b)[32]) { tmem_ld32x2(t, t + 32, a, b); }
 
 // 64 consecutive fp32 accumulator columns of this thread's TMEM lane (one tcgen05.ld).
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
