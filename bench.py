@@ -304,6 +304,23 @@ def main():
                 "algorithmic_bytes_per_launch": 2.0 * tok_ns * L * (10 * Hh + 2 * I) / gemm_launches,
                 "flops_per_launch": gemm_flops / gemm_launches, "ms_per_launch": gemm_ms / gemm_launches}
     stage_ms = {k: v[0] / ns for k, v in st.items() if v[1]}
+    # HBM-bound kernels: algorithmic bytes of the stage-timing forwards / their event time.
+    es = 4 if w.dtype == "f32" else 2
+    seqs_ns = sum(len(batches[i % nb][1]) for i in range(ns))
+    hbm_bytes = {
+        # LayerNorm (2 per layer): read the residual-stream rows, write the normalised rows.
+        "layernorm": 2.0 * L * tok_ns * Hh * es * 2,
+        # embed: word row (+ position row for absolute positions) read, output row written.
+        "embed": tok_ns * Hh * es * (3 if cfg.rope_base == 0 else 2),
+        # mean-pool + L2: read every token row, write B fp32 vectors.
+        "pool": tok_ns * Hh * es + seqs_ns * Hh * 4,
+    }
+    hbm_kernels = {}
+    for k, nbytes in hbm_bytes.items():
+        if k in st and st[k][1]:
+            gbs = nbytes / (st[k][0] / 1000) / 1e9
+            hbm_kernels[k] = {"achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                              "bytes_per_step": nbytes / ns}
 
     # ---- end to end through the host entry point (pinned host buffers)
     pin_ids = [torch.from_numpy(ids).pin_memory().numpy() for ids, _ in batches]
@@ -371,6 +388,7 @@ def main():
             "tokens_per_step": tokens / args.steps,
             "model_tflops": flops * world / (ms_max / 1000) / 1e12,
             "roofline": roofline,
+            "hbm_kernels": hbm_kernels,
             "stage_ms_per_step": stage_ms,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "vectors/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
