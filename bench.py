@@ -311,7 +311,7 @@ def main():
         # LayerNorm (2 per layer): read the residual-stream rows, write the normalised rows.
         "layernorm": 2.0 * L * tok_ns * Hh * es * 2,
         # embed: word row (+ position row for absolute positions) read, output row written.
-        "embed": tok_ns * Hh * es * (3 if cfg.rope_base == 0 else 2),
+        "embed": tok_ns * Hh * es * (3 if cfg.position_type == synth.POS_ABSOLUTE else 2),
         # mean-pool + L2: read every token row, write B fp32 vectors.
         "pool": tok_ns * Hh * es + seqs_ns * Hh * 4,
     }
