@@ -200,6 +200,8 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=4, help="sequences per step for the CPU reference")
     ap.add_argument("--cpu-sample", type=int, default=8, help="sequences in the cpu_baseline sample")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--gather", action="store_true",
+                    help="N>1: all-gather every step's pooled vectors to all ranks over NCCL inside the timed region")
     ap.add_argument("--lat-iters", type=int, default=50, help="single-request latency samples")
     ap.add_argument("--requests", type=int, default=20000, help="cfg5: requests in the sample")
     ap.add_argument("--clients", type=int, default=256, help="cfg5: concurrent closed-loop clients")
@@ -237,9 +239,16 @@ def main():
     d_out = torch.empty((w.batch, H), dtype=torch.float32, device=f"cuda:{local}")
     torch.cuda.synchronize()
 
+    gather = args.gather and world > 1
+    if gather:
+        import replicas
+
     def step(i):
         ids, lens = batches[i % nb]
         model.forward_batch_device(d_ids[i % nb].data_ptr(), lens, fl.POOL_MEAN_L2, d_out.data_ptr())
+        if gather:  # optional NCCL gather of the pooled vectors, ordered on the library stream
+            with torch.cuda.stream(stream):
+                replicas.gather_pooled(d_out, rank * w.batch, world * w.batch)
 
     # Preparation (untimed): each batch shape twice, so that its CUDA graph is captured before
     # the warm-up and timed steps (the library captures a shape on its second occurrence).
@@ -383,7 +392,8 @@ def main():
             "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
             "config": {"workload": f"{args.workload}: {w.name}, lengths {w.dist} [{w.len_lo},{w.len_hi}], packed varlen, "
                                    "mean pool + L2", "global_batch": w.batch * world, "seq_len": w.len_hi,
-                       "parallelism": f"replicas x{world} (no collective)",
+                       "parallelism": (f"replicas x{world}, NCCL all-gather of the pooled vectors per step" if gather
+                                       else f"replicas x{world} (no collective)"),
                        "l2": "inputs larger than L2: 0.27 GB weights + ~1 GB activations streamed per step"},
             "tokens_per_step": tokens / args.steps,
             "model_tflops": flops * world / (ms_max / 1000) / 1e12,

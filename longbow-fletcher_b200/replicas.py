@@ -81,3 +81,35 @@ def shard_rows(lengths, ranges):
     """Token offsets [t0, t1) of each sequence range in the packed id array."""
     cu = np.concatenate([[0], np.cumsum(np.asarray(lengths, np.int64))])
     return [(int(cu[a]), int(cu[b])) for a, b in ranges]
+
+
+def gather_pooled(vectors, offset, total, group=None):
+    """Collects every rank's pooled vectors into one [total, H] array in request order.
+
+    Rank r holds rows [offset_r, offset_r + n_r) of the request (`vectors` is [n_r, H], a torch
+    tensor on the rank's device: CUDA for NCCL, CPU for gloo).  The ranks' row counts may
+    differ, so counts and offsets are exchanged first and every block is padded to the largest
+    count for one all_gather.  This is the optional gather of the survey's multi-GPU plan; the
+    forward itself needs no collective.  Returns the full array on every rank (torch tensor).
+    """
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    dev = vectors.device
+    meta = torch.tensor([vectors.shape[0], offset], dtype=torch.int64, device=dev)
+    metas = [torch.empty_like(meta) for _ in range(world)]
+    dist.all_gather(metas, meta, group=group)
+    counts = [int(m[0]) for m in metas]
+    offs = [int(m[1]) for m in metas]
+    width = vectors.shape[1]
+    cap = max(max(counts), 1)
+    pad = torch.zeros((cap, width), dtype=vectors.dtype, device=dev)
+    pad[:vectors.shape[0]] = vectors
+    blocks = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(blocks, pad, group=group)
+    out = torch.zeros((total, width), dtype=vectors.dtype, device=dev)
+    for r in range(world):
+        if counts[r]:
+            out[offs[r]:offs[r] + counts[r]] = blocks[r][:counts[r]]
+    return out

@@ -52,17 +52,13 @@ def _worker(rank, world, port, q):
     ids = synth.make_ids(lens, cfg.vocab_size, 3)
     ranges = replicas.split_by_weight(lens, [1.0] * world)
     rows = replicas.shard_rows(lens, ranges)
-    mine = None
+    import torch
+    vec, off = torch.zeros((0, cfg.hidden)), 0
     if rank < len(ranges):
         (a, b), (t0, t1) = ranges[rank], rows[rank]
-        mine = (a, oracle.forward(cfg, blob, ids[t0:t1], lens[a:b], threads=1)["mean"])
-    parts = [None] * world
-    dist.all_gather_object(parts, mine)
+        vec, off = torch.from_numpy(oracle.forward(cfg, blob, ids[t0:t1], lens[a:b], threads=1)["mean"]), a
+    out = replicas.gather_pooled(vec, off, len(lens)).numpy()  # unequal row counts per rank
     if rank == 0:
-        out = np.zeros((len(lens), cfg.hidden), np.float32)
-        for p in parts:
-            if p is not None:
-                out[p[0]:p[0] + len(p[1])] = p[1]
         full = oracle.forward(cfg, blob, ids, lens, threads=1)["mean"]
         q.put(float(np.abs(out - full).max()))
     dist.barrier()
