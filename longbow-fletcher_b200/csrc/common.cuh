@@ -23,6 +23,8 @@ struct Ctx {
   int64_t allocated = 0;
   int32_t* d_err = nullptr;  // device flag, set by kernels on a bounded-wait timeout
   int64_t launches = 0;      // kernels launched on this context (counted by FL_LAUNCH)
+  float* splitk = nullptr;   // split-K workspace of small-M GEMMs, lent by the running model
+  int64_t splitk_bytes = 0;
   std::string last_error;
 };
 

@@ -10,7 +10,8 @@ enum Epi : int {
   EPI_ROPE = 1,     // out = rope(acc + bias) on columns < rope_cols (head_dim 64), pos[row]
   EPI_GELU = 2,     // out = GeluFast(acc + bias)
   EPI_SWIGLU = 3,   // out[:, j] = silu(gate + bg) * (up + bu), W packed gate/up-interleaved
-  EPI_RESIDUAL = 4  // out = acc + bias + residual
+  EPI_RESIDUAL = 4,  // out = acc + bias + residual
+  EPI_PARTIAL = 5    // internal (split-K): fp32 sums of one K range to a workspace, finished later
 };
 
 struct GemmArgs {
@@ -27,9 +28,17 @@ struct GemmArgs {
   const float* sin_t;
   int64_t rope_cols;
   int32_t* err;
+  int splits;      // K ranges per output tile (1 unless EPI_PARTIAL)
+  int kb_per;      // 64-wide K blocks per range
+  float* partial;  // EPI_PARTIAL: [splits, M, N] fp32
 };
 
 bool gemm_tc_supported(int64_t M, int64_t N, int64_t K, int bn);
+
+// Split-K for GEMMs with few output tiles: the plan's fp32 workspace bytes (0 = no split).  A
+// launch splits only when the context's workspace (Ctx::splitk, lent by the model that owns
+// it) is large enough; launches never allocate.
+int64_t gemm_splitk_plan(const Ctx* c, int64_t M, int64_t N, int64_t K, int* splits, int* kb_per);
 
 // A: [M, K] row-major 16-bit; W: [N, K] (K-major) 16-bit; bias fp32 [N] (packed order) or null.
 int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, int64_t M, int64_t K, const void* W,

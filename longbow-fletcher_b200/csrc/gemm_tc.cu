@@ -43,7 +43,7 @@ constexpr int kStageOut = 32 * 128;                    // per-warp output box: 3
 constexpr int kOutBufs = 2;                            // output boxes in flight per warp
 // Epilogues drained by alternating warp groups (see the epilogue section of k_gemm_tc).
 template <int EPI>
-constexpr bool kEpiGroups = EPI == 0 || EPI == 1 || EPI == 2;  // EPI_STORE, EPI_ROPE, EPI_GELU
+constexpr bool kEpiGroups = EPI == 0 || EPI == 1 || EPI == 2 || EPI == 5;  // STORE, ROPE, GELU, PARTIAL
 
 // PAIR: the tile is computed by a cluster of two CTAs on two SMs with tcgen05 cta_group::2
 // (M = 256 per MMA): each CTA loads its 128 rows of A and half of the tile's BN rows of W, and
@@ -124,8 +124,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = args.num_n_tiles;
-  const int num_tiles = args.num_m_tiles * n_tiles;
+  const int splits = args.splits;  // K ranges per output tile (split-K partial sums)
+  const int num_tiles = args.num_m_tiles * n_tiles * splits;
   const int num_kb = args.K / BK;
+  auto kb_range = [&](int tile, int& kb0, int& kb1) {
+    kb0 = (tile % splits) * args.kb_per;
+    kb1 = kb0 + args.kb_per < num_kb ? kb0 + args.kb_per : num_kb;
+  };
   // Pair mode: clusters of two consecutive CTAs; CTA rank 0 issues the MMAs.
   const uint32_t crank = PAIR ? cluster_ctarank() : 0;
   const int first_tile = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
@@ -175,10 +180,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
-        const int mb = tile / n_tiles, nb = tile % n_tiles;
+        const int mb = tile / splits / n_tiles, nb = tile / splits % n_tiles;
+        int kb0, kb1;
+        kb_range(tile, kb0, kb1);
         const int a_row = mb * C::TILE_M + (int)crank * BM;
         const int b_row = nb * BN + (int)crank * C::B_ROWS;
-        for (int kb = 0; kb < num_kb; kb++) {
+        for (int kb = kb0; kb < kb1; kb++) {
           if (!mbar_wait_spin(&empty[stage], phase ^ 1, abort, args.err)) goto producer_done;
           if constexpr (PAIR) {
             // Both CTAs' loads complete on the even CTA's barrier, which expects both.
@@ -212,7 +219,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < num_kb; kb++) {
+        int kb0, kb1;
+        kb_range(tile, kb0, kb1);
+        for (int kb = kb0; kb < kb1; kb++) {
           if (!mbar_wait_spin(&full[stage], phase, abort, args.err)) {
             ok = false;
             break;
@@ -223,9 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; k++) {  // +32 bytes per K=16 step inside the swizzle atom
             if constexpr (PAIR)
-              mma_f16_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, id, (kb | k) != 0);
+              mma_f16_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, id, (kb > kb0 || k > 0) ? 1u : 0u);
             else
-              mma_f16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, id, (kb | k) != 0);
+              mma_f16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, id, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           if constexpr (PAIR)
             mma_commit_pair(&empty[stage]);  // frees the stage in both CTAs
@@ -263,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = grp;
     const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0;
     auto tile_row = [&](int t) -> int64_t {
-      return (int64_t)(t / n_tiles) * C::TILE_M + (int)crank * BM + q * 32 + lane;
+      return (int64_t)(t / splits / n_tiles) * C::TILE_M + (int)crank * BM + q * 32 + lane;
     };
     // RoPE positions run one tile ahead, so a tile's table loads need no dependent load.
     const int t0 = first_tile + grp * tile_stride;
@@ -272,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (t0 < num_tiles && tile_row(t0) < args.M) pos_next = args.pos[tile_row(t0)];
     }
     for (int tile = t0; tile < num_tiles; tile += tstep * tile_stride, it += tstep) {
-      const int mb = tile / n_tiles, nb = tile % n_tiles;
+      const int mb = tile / splits / n_tiles, nb = tile / splits % n_tiles;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       const int row0 = mb * C::TILE_M + (int)crank * BM + q * 32;
@@ -395,7 +404,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               mbar_arrive(&tempty[acc]);
           }
         }
-        if (ocol < n_out && row0 < args.M) {
+        if constexpr (EPI == EPI_PARTIAL) {  // fp32 sums of this K range, 8 x 32-byte stores
+          if (ocol < args.N && row_ok) {
+            float* dst = args.partial + ((int64_t)(tile % splits) * args.M + row) * args.N + ocol;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+              const float* v = c < 4 ? &a[c * 8] : &b[(c - 4) * 8];
+              asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + c * 8), "f"(v[0]),
+                           "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+                           : "memory");
+            }
+          }
+        } else if (ocol < n_out && row0 < args.M) {
           uint8_t* stg = stg0 + ob * kStageOut;
           if (lane == 0) bulk_wait_read1();  // the box stored from this buffer has left it
           __syncwarp();
@@ -426,6 +446,90 @@ __global__ void __launch_bounds__(kThreads, 1)
     else
       asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
                    : "memory");
+  }
+}
+
+// Split-K finish: out = epilogue(sum over splits of the fp32 partial sums), the same epilogues
+// as the tensor-core kernel (same formulas, same packed column order for SwiGLU).  One thread
+// per output pair: columns (2i, 2i+1), or for RoPE a head's (c, c+32), or for SwiGLU the gate /
+// up columns of two outputs.
+template <typename T, int EPI>
+__global__ void __launch_bounds__(256)
+    k_splitk_finish(const float* __restrict__ part, int splits, int64_t M, int64_t N, T* __restrict__ out,
+                    int64_t ld_out, const float* __restrict__ bias, const T* __restrict__ res, int64_t ld_res,
+                    const int32_t* __restrict__ pos, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                    int64_t rope_cols) {
+  const int64_t n_out = EPI == EPI_SWIGLU ? N / 2 : N;
+  const int64_t pairs = M * (n_out / 2);
+  const int64_t plane = M * N;
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = p / (n_out / 2);
+    const int64_t k = p % (n_out / 2);
+    // Packed columns read (c0, c1) and the output columns written (o0, o1).
+    int64_t c0, c1, o0, o1;
+    if constexpr (EPI == EPI_ROPE) {
+      c0 = (k / 32) * 64 + k % 32;  // x1 and x2 of one rotate-half pair
+      c1 = c0 + 32;
+      o0 = c0;
+      o1 = c1;
+    } else {
+      o0 = 2 * k;
+      o1 = o0 + 1;
+      c0 = o0;
+      c1 = o1;
+    }
+    const float* pr = part + row * N;
+    if constexpr (EPI == EPI_SWIGLU) {
+      // Output j: gate column (j/128)*256 + j%128, up column gate + 128 (the weight packing).
+      float y[2];
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int64_t j = o0 + e;
+        const int64_t gcol = (j / 128) * 256 + j % 128, ucol = gcol + 128;
+        float g = 0.f, v = 0.f;
+        for (int sp = 0; sp < splits; sp++) {
+          g += pr[sp * plane + gcol];
+          v += pr[sp * plane + ucol];
+        }
+        if (bias) {
+          g += bias[gcol];
+          v += bias[ucol];
+        }
+        y[e] = __fdividef(g, 1.0f + __expf(-g)) * v;
+      }
+      *reinterpret_cast<uint32_t*>(out + row * ld_out + o0) = pack2<T>(y[0], y[1]);
+    } else {
+      float a = 0.f, b = 0.f;
+      for (int sp = 0; sp < splits; sp++) {
+        a += pr[sp * plane + c0];
+        b += pr[sp * plane + c1];
+      }
+      if (bias) {
+        a += bias[c0];
+        b += bias[c1];
+      }
+      if constexpr (EPI == EPI_ROPE) {
+        if (c0 < rope_cols) {
+          const int i = (int)(k % 32);
+          const float cs = cos_t[(int64_t)pos[row] * 32 + i], sn = sin_t[(int64_t)pos[row] * 32 + i];
+          const float x1 = a, x2 = b;
+          a = x1 * cs - x2 * sn;
+          b = x1 * sn + x2 * cs;
+        }
+        out[row * ld_out + o0] = from_f<T>(a);
+        out[row * ld_out + o1] = from_f<T>(b);
+      } else {
+        if constexpr (EPI == EPI_GELU) {
+          a = gelu_fast(a);
+          b = gelu_fast(b);
+        }
+        if constexpr (EPI == EPI_RESIDUAL) {
+          a += to_f<T>(res[row * ld_res + o0]);
+          b += to_f<T>(res[row * ld_res + o1]);
+        }
+        *reinterpret_cast<uint32_t*>(out + row * ld_out + o0) = pack2<T>(a, b);
+      }
+    }
   }
 }
 
@@ -471,7 +575,7 @@ static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const C
   }
   a.num_m_tiles = (int)((a.M + Cf::TILE_M - 1) / Cf::TILE_M);
   a.num_n_tiles = (int)((a.N + BN - 1) / BN);
-  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  const int tiles = a.num_m_tiles * a.num_n_tiles * a.splits;
   if constexpr (PAIR) {
     const int pairs = c->num_sms / 2;
     cudaLaunchConfig_t cfg = {};
@@ -508,6 +612,8 @@ static int32_t dispatch(Ctx* c, int epi, int bn, const CUtensorMap& ma, const CU
     FL_EPI(EPI_RESIDUAL)
     case EPI_SWIGLU:
       return run<T, 256, EPI_SWIGLU, PAIR>(c, ma, mb, mc, a);
+    case EPI_PARTIAL:
+      return run<T, 128, EPI_PARTIAL, false>(c, ma, mb, mc, a);
   }
 #undef FL_EPI
   return set_error(c, FLETCHER_ERR_INVALID, "gemm: unknown epilogue %d", epi);
@@ -529,6 +635,80 @@ bool gemm_pair_enabled() {
   return on;
 }
 
+// Split-K plan for a GEMM whose output tiles (128 x 128) cannot fill the GPU: K ranges per tile
+// such that tiles x ranges reaches about one CTA per SM, at least two 64-wide K blocks each.
+// Returns the fp32 workspace bytes ([splits, M, N]), 0 when no split is worthwhile.
+int64_t gemm_splitk_plan(const Ctx* c, int64_t M, int64_t N, int64_t K, int* splits, int* kb_per) {
+  const int64_t tiles = ((M + 127) / 128) * ((N + 127) / 128);
+  const int kb = (int)(K / tc::BK);
+  if (M > 1024 || tiles * 2 > c->num_sms || kb < 4 || N % 128 != 0) return 0;
+  int sp = (int)((c->num_sms + tiles - 1) / tiles);
+  if (sp > kb / 2) sp = kb / 2;
+  const int per = (kb + sp - 1) / sp;
+  sp = (kb + per - 1) / per;
+  if (sp < 2) return 0;
+  *splits = sp;
+  *kb_per = per;
+  return (int64_t)sp * M * N * 4;
+}
+
+// Partial-sum GEMM (tcgen05, 128 x 128 tiles, `splits` K ranges) + finishing epilogue kernel.
+static int32_t launch_gemm_splitk(Ctx* c, int32_t dtype, int epi, const void* A, int64_t M, int64_t K, const void* W,
+                                  int64_t N, void* out, int64_t ld_out, const float* bias, const void* residual,
+                                  int64_t ld_res, const int32_t* pos, const float* cos_t, const float* sin_t,
+                                  int64_t rope_cols, int splits, int kb_per) {
+  CUtensorMap ma, mb;
+  int32_t rc = tc::make_map(c, &ma, dtype, A, (uint64_t)M, (uint64_t)K, (uint64_t)K, tc::BK, tc::BM);
+  if (rc) return rc;
+  if ((rc = tc::make_map(c, &mb, dtype, W, (uint64_t)N, (uint64_t)K, (uint64_t)K, tc::BK, 128))) return rc;
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = (int)K;
+  a.err = c->d_err;
+  a.splits = splits;
+  a.kb_per = kb_per;
+  a.partial = c->splitk;
+  if (dtype == FLETCHER_BF16)
+    rc = tc::dispatch<__nv_bfloat16, false>(c, EPI_PARTIAL, 128, ma, mb, ma, a);
+  else
+    rc = tc::dispatch<__half, false>(c, EPI_PARTIAL, 128, ma, mb, ma, a);
+  if (rc) return rc;
+  const int64_t n_out = epi == EPI_SWIGLU ? N / 2 : N;
+  const int64_t pairs = M * (n_out / 2);
+  const int grid = (int)std::min<int64_t>((pairs + 255) / 256, (int64_t)c->num_sms * 8);
+#define FL_FIN(TT, E)                                                                                          \
+  tc::k_splitk_finish<TT, E><<<grid, 256, 0, c->stream>>>(c->splitk, splits, M, N, (TT*)out, ld_out, bias,  \
+                                                          (const TT*)residual, ld_res, pos, cos_t, sin_t, rope_cols)
+#define FL_FIN_T(TT)                 \
+  switch (epi) {                     \
+    case EPI_STORE:                  \
+      FL_FIN(TT, EPI_STORE);         \
+      break;                         \
+    case EPI_ROPE:                   \
+      FL_FIN(TT, EPI_ROPE);          \
+      break;                         \
+    case EPI_GELU:                   \
+      FL_FIN(TT, EPI_GELU);          \
+      break;                         \
+    case EPI_SWIGLU:                 \
+      FL_FIN(TT, EPI_SWIGLU);        \
+      break;                         \
+    default:                         \
+      FL_FIN(TT, EPI_RESIDUAL);      \
+      break;                         \
+  }
+  if (dtype == FLETCHER_BF16) {
+    FL_FIN_T(__nv_bfloat16)
+  } else {
+    FL_FIN_T(__half)
+  }
+#undef FL_FIN_T
+#undef FL_FIN
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
 bool gemm_tc_supported(int64_t M, int64_t N, int64_t K, int bn) {
   return M > 0 && M < (1ll << 31) && K % tc::BK == 0 && K > 0 && N % 64 == 0 && (bn == 128 || bn == 256);
 }
@@ -545,6 +725,15 @@ int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, in
   FL_CHECK(c, epi != EPI_RESIDUAL || (((uintptr_t)residual & 15) == 0 && ld_res % 8 == 0),
            "gemm_tc: residual must be 16-byte aligned");
   const int64_t n_out = epi == EPI_SWIGLU ? N / 2 : N;
+  // Few output tiles (small batches, single requests): split K so that enough CTAs stream the
+  // weights, then finish the sums with the epilogue in a second kernel.
+  {
+    int splits = 0, kb_per = 0;
+    const int64_t need = gemm_splitk_plan(c, M, N, K, &splits, &kb_per);
+    if (need > 0 && need <= c->splitk_bytes)
+      return launch_gemm_splitk(c, dtype, epi, A, M, K, W, N, out, ld_out, bias, residual, ld_res, pos, cos_t, sin_t,
+                                rope_cols, splits, kb_per);
+  }
   // CTA pairs (2-SM MMAs) once there are enough 256-row tiles to fill the GPU.
   const bool pair = gemm_pair_enabled() && M >= 2048;
   CUtensorMap ma, mb, mc;
@@ -568,6 +757,8 @@ int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, in
   a.sin_t = sin_t;
   a.rope_cols = rope_cols;
   a.err = c->d_err;
+  a.splits = 1;
+  a.kb_per = (int)(K / tc::BK);
   if (pair) {
     if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16, true>(c, epi, bn, ma, mb, mc, a);
     return tc::dispatch<__half, true>(c, epi, bn, ma, mb, mc, a);

@@ -61,6 +61,8 @@ struct Model {
   int64_t tiles_cap = 0;
   float* d_out = nullptr;
   float* d_cls = nullptr;
+  float* splitk = nullptr;  // split-K partial sums of the GEMMs of small batches
+  int64_t splitk_bytes = 0;
   std::vector<std::pair<void*, int64_t>> ws;
   // pinned staging for per-batch metadata
   uint8_t* h_meta = nullptr;
@@ -99,6 +101,10 @@ void clear_graphs(Model* m);
 
 static void free_ws(Model* m) {
   clear_graphs(m);  // captured graphs hold the old workspace pointers
+  if (m->splitk && m->c->splitk == m->splitk) {  // stop lending the split-K workspace
+    m->c->splitk = nullptr;
+    m->c->splitk_bytes = 0;
+  }
   for (auto& a : m->ws) dev_free(m->c, a.first, a.second);
   m->ws.clear();
   m->ws_T = 0;
@@ -130,6 +136,22 @@ static int32_t ensure_ws(Model* m, int64_t T, int32_t B) {
   if ((rc = ws_alloc(m, (void**)&m->d_tiles, m->tiles_cap * 8))) return rc;
   if ((rc = ws_alloc(m, (void**)&m->d_out, Bc * m->H * 4))) return rc;
   if ((rc = ws_alloc(m, (void**)&m->d_cls, Bc * m->H * 4))) return rc;
+  // Split-K workspace: the largest plan of the four GEMM shapes for batches of up to 1024 tokens.
+  m->splitk = nullptr;
+  m->splitk_bytes = 0;
+  if (m->dtype != FLETCHER_F32) {
+    const int64_t shapes[4][2] = {{3 * m->H, m->H}, {m->H, m->H}, {m->Iup, m->H}, {m->H, m->I}};  // N, K
+    int64_t need = 0;
+    for (int64_t M = 128; M <= std::min<int64_t>(Tc, 1024); M += 128)
+      for (const auto& sh : shapes) {
+        int sp = 0, per = 0;
+        need = std::max(need, gemm_splitk_plan(m->c, M, sh[0], sh[1], &sp, &per));
+      }
+    if (need > 0) {
+      if ((rc = ws_alloc(m, (void**)&m->splitk, need))) return rc;
+      m->splitk_bytes = need;
+    }
+  }
   m->ws_T = Tc;
   m->ws_B = (int32_t)Bc;
   return FLETCHER_OK;
@@ -390,6 +412,8 @@ static int32_t forward_device(Model* m, const int32_t* d_ids, const int32_t* len
   if ((rc = upload_meta(m, lengths, B, T, &n_tiles, &max_len))) return rc;
   if ((rc = ensure_rope(m, max_len))) return rc;
   m->last_T = T;
+  c->splitk = m->splitk;  // this model's split-K workspace for its GEMM launches
+  c->splitk_bytes = m->splitk_bytes;
   return launch_or_replay(m, d_ids, lengths, B, pooling, d_out, T, n_tiles, max_len);
 }
 

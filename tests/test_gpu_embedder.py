@@ -7,6 +7,7 @@ import numpy as np
 import pytest
 
 import synth
+from helpers import assert_close_16
 
 pytestmark = pytest.mark.gpu
 
@@ -35,7 +36,9 @@ def test_embed_matches_single_replica(emb):
     want = _direct(emb, ids, lens)
     emb.replicas[0].throughput, emb.replicas[1].throughput = 3.0, 1.0  # uneven split
     got = emb.embed(ids, lens)
-    assert np.array_equal(got, want)  # packing- and batching-invariant, bit for bit
+    # Packing- and batching-invariant up to the fp32 summation order of small batches' split-K
+    # GEMMs (their number of partial sums depends on the batch's token count).
+    assert_close_16(got, want, "replicas vs one replica", cos_min=0.99999)
 
 
 def test_server_requests(emb):
@@ -52,4 +55,4 @@ def test_server_requests(emb):
     for (ids, lens), f in zip(reqs, futs):
         vecs, lat = f.result(timeout=60)
         assert lat > 0 and vecs.shape == (len(lens), CFG.hidden)
-        assert np.array_equal(vecs, _direct(emb, ids, lens))
+        assert_close_16(vecs, _direct(emb, ids, lens), "served vs direct", cos_min=0.99999)

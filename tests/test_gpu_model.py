@@ -79,17 +79,24 @@ def test_edge_lengths_nomic(be, oracle_mod, lengths, dtype):
 
 
 def test_packing_invariance_bitexact(be):
-    """A sequence's embedding does not depend on the other sequences packed with it."""
+    """A sequence's embedding does not depend on the other sequences packed with it: bit-exact
+    while the batch and the single sequence both run unsplit GEMMs (more than 1024 tokens),
+    within 16-bit tolerance when the shorter batches' GEMMs split K into a different number of
+    fp32 partial sums."""
     cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
     m = model(be, cfg, "bf16", 1)
-    lens = np.array([200, 5, 64, 129, 31], np.int32)
-    ids = synth.make_ids(lens, cfg.vocab_size, 9)
-    full = m.forward_batch(ids, lens, 1)
-    off = 0
-    for i, L in enumerate(lens):
-        single = m.forward_batch(ids[off:off + L], lens[i:i + 1], 1)
-        assert np.array_equal(single[0], full[i]), i
-        off += L
+    for lengths, exact in (([1100, 1030, 1500], True), ([200, 5, 64, 129, 31], False)):
+        lens = np.array(lengths, np.int32)
+        ids = synth.make_ids(lens, cfg.vocab_size, 9)
+        full = m.forward_batch(ids, lens, 1)
+        off = 0
+        for i, L in enumerate(lens):
+            single = m.forward_batch(ids[off:off + L], lens[i:i + 1], 1)
+            if exact:
+                assert np.array_equal(single[0], full[i]), (lengths, i)
+            else:
+                assert_close_16(single, full[i:i + 1], f"packed vs single {lengths} {i}")
+            off += L
 
 
 def test_cfg3_full_size_bf16(be, oracle_mod):

@@ -90,6 +90,37 @@ def test_linear_tensor_core(fl, be, M, K, N, act, dtype):
     assert err < (1e-2 if dtype == "bf16" else 2e-3), err
 
 
+@pytest.mark.parametrize("M,K,N,act", [(64, 768, 3072, 1), (200, 3072, 768, 0), (1, 768, 6144, 4), (300, 768, 2304, 0)])
+def test_linear_split_k(fl, be, M, K, N, act):
+    """Small-M 16-bit GEMMs split K across CTAs (fp32 partial sums + a finishing epilogue kernel)
+    once a model has lent its split-K workspace to the context; same check as above."""
+    import dataclasses
+    import synth
+    cfg = dataclasses.replace(synth.NOMIC, num_layers=1)
+    m = fl.BertModel(be, cfg, "bf16")
+    m.load_raw(synth.make_weights(cfg, 1))
+    lens = np.array([1024], np.int32)  # sizes the workspace for batches of up to 1024 tokens
+    m.forward_batch(synth.make_ids(lens, cfg.vocab_size, 1), lens, 1)
+    rng = np.random.default_rng(M + K + N)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((K, N)) * 0.05).astype(np.float32)
+    b = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    dt = fl.DTYPES["bf16"]
+    tx, tw, tb = be.new_tensor(M, K, x, dt), be.new_tensor(K, N, w, dt), be.new_tensor(1, N, b, dt)
+    got = tx.linear(tx, tw, tb, act).to_host()
+    y = bf16_round(x).astype(np.float64) @ bf16_round(w).astype(np.float64) + bf16_round(b)
+    if act == 1:
+        u = 0.7978846 * (y + 0.044715 * y ** 3)
+        th = np.where(u > 4, 1, np.where(u < -4, -1, u * (27 + u * u) / (27 + 9 * u * u)))
+        y = 0.5 * y * (1 + th)
+    elif act == 4:
+        a, c = y[:, : N // 2], y[:, N // 2:]
+        y = a / (1 + np.exp(-a)) * c
+    err = np.abs(got - y).max() / max(1e-3, np.abs(y).max())
+    assert err < 1e-2, err
+    del m
+
+
 @pytest.mark.parametrize("act", [0, 1, 2, 4])
 def test_linear_f32(fl, be, act):
     rng = np.random.default_rng(act)
