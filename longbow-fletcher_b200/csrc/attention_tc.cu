@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // the setup above overlapped the previous kernel; its outputs are visible now
 
   if (warp < kSlots) {
     // Control thread of slot `warp`: TMA loads and MMA issue with sleeping bounded waits.
@@ -435,9 +436,9 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void*
   const int want = (work + kSlots - 1) / kSlots;
   const int grid = want < 2 * c->num_sms ? want : 2 * c->num_sms;
   if (dt == FLETCHER_BF16)
-    k_attn_tc<__nv_bfloat16><<<grid, kThreads, SMEM, c->stream>>>(mq, mk, mv, a);
+    FL_CUDA(c, launch_pdl(k_attn_tc<__nv_bfloat16>, dim3(grid), dim3(kThreads), SMEM, c->stream, mq, mk, mv, a));
   else
-    k_attn_tc<__half><<<grid, kThreads, SMEM, c->stream>>>(mq, mk, mv, a);
+    FL_CUDA(c, launch_pdl(k_attn_tc<__half>, dim3(grid), dim3(kThreads), SMEM, c->stream, mq, mk, mv, a));
   FL_LAUNCH(c);
   return FLETCHER_OK;
 }

@@ -1,5 +1,6 @@
 // Shared definitions of libcuda_fletcher: context, buffers, error plumbing, dtype helpers.
 #pragma once
+#include <utility>
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -66,6 +67,29 @@ struct DeviceGuard {
       return ::fl::set_error((ctx), FLETCHER_ERR_CUDA, "kernel launch failed: %s (%s:%d)",  \
                              cudaGetErrorString(e_), __FILE__, __LINE__);                   \
   } while (0)
+
+// Programmatic dependent launch (sm_90+): a kernel launched with launch_pdl may begin while the
+// previous kernel on the stream is finishing, so its setup (barrier init, TMEM allocation,
+// tensor-map prefetch) overlaps that kernel's tail.  It must call pdl_wait() before it touches
+// global memory that an earlier kernel writes or reads; the wait returns once that kernel has
+// completed and its writes are visible.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Allocation from the stream-ordered pool; zero-filled.
 int32_t dev_alloc(Ctx* c, void** p, int64_t bytes);

@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();  // the setup above overlapped the previous kernel; its outputs are visible now
 
   if (warp == 0) {
     if (lane == 0) {
@@ -459,6 +460,7 @@ __global__ void __launch_bounds__(256)
                     int64_t ld_out, const float* __restrict__ bias, const T* __restrict__ res, int64_t ld_res,
                     const int32_t* __restrict__ pos, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                     int64_t rope_cols) {
+  pdl_wait();
   const int64_t n_out = EPI == EPI_SWIGLU ? N / 2 : N;
   const int64_t pairs = M * (n_out / 2);
   const int64_t plane = M * N;
@@ -583,17 +585,19 @@ static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const C
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = Cf::SMEM;
     cfg.stream = c->stream;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 2;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     FL_CUDA(c, cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, a));
   } else {
     const int grid = tiles < c->num_sms ? tiles : c->num_sms;
-    kern<<<grid, kThreads, Cf::SMEM, c->stream>>>(ma, mb, mc, a);
+    FL_CUDA(c, launch_pdl(kern, dim3(grid), dim3(kThreads), Cf::SMEM, c->stream, ma, mb, mc, a));
   }
   FL_LAUNCH(c);
   return FLETCHER_OK;
@@ -677,9 +681,9 @@ static int32_t launch_gemm_splitk(Ctx* c, int32_t dtype, int epi, const void* A,
   const int64_t n_out = epi == EPI_SWIGLU ? N / 2 : N;
   const int64_t pairs = M * (n_out / 2);
   const int grid = (int)std::min<int64_t>((pairs + 255) / 256, (int64_t)c->num_sms * 8);
-#define FL_FIN(TT, E)                                                                                          \
-  tc::k_splitk_finish<TT, E><<<grid, 256, 0, c->stream>>>(c->splitk, splits, M, N, (TT*)out, ld_out, bias,  \
-                                                          (const TT*)residual, ld_res, pos, cos_t, sin_t, rope_cols)
+#define FL_FIN(TT, E)                                                                                         \
+  FL_CUDA(c, launch_pdl(tc::k_splitk_finish<TT, E>, dim3(grid), dim3(256), 0, c->stream, (const float*)c->splitk, \
+                        splits, M, N, (TT*)out, ld_out, bias, (const TT*)residual, ld_res, pos, cos_t, sin_t, rope_cols))
 #define FL_FIN_T(TT)                 \
   switch (epi) {                     \
     case EPI_STORE:                  \

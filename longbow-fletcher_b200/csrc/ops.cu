@@ -57,6 +57,7 @@ template <typename T, int PER, int VEC>
 __global__ void __launch_bounds__(128) k_add_ln(const T* __restrict__ x, const T* __restrict__ res, T* out,
                                                 const float* __restrict__ g, const float* __restrict__ b,
                                                 int64_t rows, int cols, float eps) {
+  pdl_wait();
   const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -120,7 +121,8 @@ static int32_t add_ln_t(Ctx* c, const T* x, const T* res, T* out, const float* g
   constexpr int V16 = sizeof(T) == 2 ? 8 : 4;
   bool done = true;
   if (cols % 32 != 0) done = false;
-#define FL_LN(PER_, VEC_) k_add_ln<T, PER_, VEC_><<<grid, 128, 0, c->stream>>>(x, res, out, g, b, rows, (int)cols, eps)
+#define FL_LN(PER_, VEC_) \
+  FL_CUDA(c, launch_pdl(k_add_ln<T, PER_, VEC_>, dim3(grid), dim3(128), 0, c->stream, x, res, out, g, b, rows, (int)cols, eps))
   else if (per == 24 && cols % (32 * V16) == 0) FL_LN(24, V16);
   else if (per == 32 && cols % (32 * V16) == 0) FL_LN(32, V16);
   else if (per == 16 && cols % (32 * V16) == 0) FL_LN(16, V16);
@@ -154,6 +156,7 @@ __global__ void __launch_bounds__(128) k_embed(const int32_t* __restrict__ ids, 
                                                const T* __restrict__ type0, const float* __restrict__ g,
                                                const float* __restrict__ b, T* __restrict__ out, int64_t rows,
                                                int cols, float eps) {
+  pdl_wait();
   const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -207,7 +210,9 @@ static int32_t embed_t(Ctx* c, const int32_t* ids, const int32_t* pos, const T* 
   constexpr int V16 = sizeof(T) == 2 ? 8 : 4;
   const int per = (int)(cols / 32);
   bool done = cols % 32 == 0;
-#define FL_EM(PER_, VEC_) k_embed<T, PER_, VEC_><<<grid, 128, 0, c->stream>>>(ids, pos, word, ptab, max_pos, type0, g, b, out, rows, (int)cols, eps)
+#define FL_EM(PER_, VEC_)                                                                                     \
+  FL_CUDA(c, launch_pdl(k_embed<T, PER_, VEC_>, dim3(grid), dim3(128), 0, c->stream, ids, pos, word, ptab, max_pos, \
+                        type0, g, b, out, rows, (int)cols, eps))
   if (!done) {
   } else if (per == 24 && cols % (32 * V16) == 0) FL_EM(24, V16);
   else if (per == 32 && cols % (32 * V16) == 0) FL_EM(32, V16);
@@ -241,6 +246,7 @@ int32_t launch_embed(Ctx* c, int32_t dt, const int32_t* ids, const int32_t* pos,
 
 // ---------------------------------------------------------------- positions
 __global__ void k_positions(const int32_t* __restrict__ cu, int32_t* __restrict__ pos) {
+  pdl_wait();
   const int s = blockIdx.x;
   const int a = cu[s], e = cu[s + 1];
   for (int i = a + threadIdx.x; i < e; i += blockDim.x) pos[i] = i - a;
@@ -248,7 +254,7 @@ __global__ void k_positions(const int32_t* __restrict__ cu, int32_t* __restrict_
 
 int32_t launch_positions(Ctx* c, const int32_t* cu, int32_t B, int32_t* pos, int32_t) {
   if (B <= 0) return FLETCHER_OK;
-  k_positions<<<B, 256, 0, c->stream>>>(cu, pos);
+  FL_CUDA(c, launch_pdl(k_positions, dim3(B), dim3(256), 0, c->stream, cu, pos));
   FL_LAUNCH(c);
   return FLETCHER_OK;
 }
@@ -259,6 +265,7 @@ int32_t launch_positions(Ctx* c, const int32_t* cu, int32_t B, int32_t* pos, int
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) k_mean_pool_l2(const T* __restrict__ h, const int32_t* __restrict__ cu,
                                                       int H, float* __restrict__ out) {
+  pdl_wait();
   extern __shared__ float part[];  // [RG][H]
   __shared__ float red[8];
   const int s = blockIdx.x;
@@ -308,10 +315,11 @@ static int32_t mean_pool_t(Ctx* c, const T* h, const int32_t* cu, int B, int64_t
   if (vec) {
     const int CG = (int)(H / V);
     const int RG = 256 / CG;
-    k_mean_pool_l2<T, V><<<B, 256, (size_t)RG * H * 4, c->stream>>>(h, cu, (int)H, out);
+    FL_CUDA(c, launch_pdl(k_mean_pool_l2<T, V>, dim3(B), dim3(256), (size_t)RG * H * 4, c->stream, h, cu, (int)H, out));
   } else {
     FL_CHECK(c, H <= 16384, "MeanPoolL2: hidden %lld too large", (long long)H);
-    k_mean_pool_l2<T, 1><<<B, 256, (size_t)(H < 256 ? 256 / H : 1) * H * 4, c->stream>>>(h, cu, (int)H, out);
+    FL_CUDA(c, launch_pdl(k_mean_pool_l2<T, 1>, dim3(B), dim3(256), (size_t)(H < 256 ? 256 / H : 1) * H * 4, c->stream,
+                          h, cu, (int)H, out));
   }
   FL_LAUNCH(c);
   return FLETCHER_OK;
