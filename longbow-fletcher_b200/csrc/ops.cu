@@ -261,13 +261,15 @@ int32_t launch_positions(Ctx* c, const int32_t* cu, int32_t B, int32_t* pos, int
 
 // ---------------------------------------------------------------- mean pool + L2
 // One block per sequence.  Threads split into column groups (VEC columns each, 128-bit loads)
-// and row groups; partial sums meet in shared memory, then the L2 norm is a block reduction.
+// and row groups; each thread keeps four row loads in flight; partial sums meet in shared
+// memory, then the L2 norm is a block reduction.
+constexpr int kPoolThreads = 512;
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256) k_mean_pool_l2(const T* __restrict__ h, const int32_t* __restrict__ cu,
+__global__ void __launch_bounds__(kPoolThreads) k_mean_pool_l2(const T* __restrict__ h, const int32_t* __restrict__ cu,
                                                       int H, float* __restrict__ out) {
   pdl_wait();
   extern __shared__ float part[];  // [RG][H]
-  __shared__ float red[8];
+  __shared__ float red[kPoolThreads / 32];
   const int s = blockIdx.x;
   const int a = cu[s], e = cu[s + 1];
   const int CG = H / VEC;
@@ -279,7 +281,17 @@ __global__ void __launch_bounds__(256) k_mean_pool_l2(const T* __restrict__ h, c
       float acc[VEC];
 #pragma unroll
       for (int i = 0; i < VEC; i++) acc[i] = 0.f;
-      for (int r = a + rg; r < e; r += RG) {
+      int r = a + rg;
+      for (; r + 3 * RG < e; r += 4 * RG) {  // four independent row loads in flight
+        Vec<T, VEC> x[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) x[u] = *reinterpret_cast<const Vec<T, VEC>*>(h + (int64_t)(r + u * RG) * H + cg * VEC);
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+          for (int i = 0; i < VEC; i++) acc[i] += to_f<T>(x[u].d[i]);
+      }
+      for (; r < e; r += RG) {
         Vec<T, VEC> x = *reinterpret_cast<const Vec<T, VEC>*>(h + (int64_t)r * H + cg * VEC);
 #pragma unroll
         for (int i = 0; i < VEC; i++) acc[i] += to_f<T>(x.d[i]);
@@ -310,16 +322,17 @@ __global__ void __launch_bounds__(256) k_mean_pool_l2(const T* __restrict__ h, c
 template <typename T>
 static int32_t mean_pool_t(Ctx* c, const T* h, const int32_t* cu, int B, int64_t H, float* out) {
   constexpr int V = sizeof(T) == 2 ? 8 : 4;
-  const bool vec = H % V == 0 && H / V <= 256;
+  const bool vec = H % V == 0 && H / V <= kPoolThreads;
   if (B <= 0) return FLETCHER_OK;
   if (vec) {
     const int CG = (int)(H / V);
-    const int RG = 256 / CG;
-    FL_CUDA(c, launch_pdl(k_mean_pool_l2<T, V>, dim3(B), dim3(256), (size_t)RG * H * 4, c->stream, h, cu, (int)H, out));
+    const int RG = kPoolThreads / CG;
+    FL_CUDA(c, launch_pdl(k_mean_pool_l2<T, V>, dim3(B), dim3(kPoolThreads), (size_t)RG * H * 4, c->stream, h, cu,
+                          (int)H, out));
   } else {
-    FL_CHECK(c, H <= 16384, "MeanPoolL2: hidden %lld too large", (long long)H);
-    FL_CUDA(c, launch_pdl(k_mean_pool_l2<T, 1>, dim3(B), dim3(256), (size_t)(H < 256 ? 256 / H : 1) * H * 4, c->stream,
-                          h, cu, (int)H, out));
+    FL_CHECK(c, H <= 8192, "MeanPoolL2: hidden %lld too large", (long long)H);
+    FL_CUDA(c, launch_pdl(k_mean_pool_l2<T, 1>, dim3(B), dim3(kPoolThreads),
+                          (size_t)(H < kPoolThreads ? kPoolThreads / H : 1) * H * 4, c->stream, h, cu, (int)H, out));
   }
   FL_LAUNCH(c);
   return FLETCHER_OK;
