@@ -198,7 +198,7 @@ def main():
     ap.add_argument("--impl", default="fletcher", choices=["fletcher", "reference"])
     ap.add_argument("--workload", default="cfg3", choices=sorted(synth.WORKLOADS) + ["cfg5"])
     ap.add_argument("--ref-sample", type=int, default=4, help="sequences per step for the CPU reference")
-    ap.add_argument("--cpu-sample", type=int, default=8, help="sequences in the cpu_baseline sample")
+    ap.add_argument("--cpu-sample", type=int, default=24, help="sequences in the cpu_baseline sample (~15 s of CPU work at cfg3)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--gather", action="store_true",
                     help="N>1: all-gather every step's pooled vectors to all ranks over NCCL inside the timed region")
