@@ -155,7 +155,10 @@ def run_server_mix(args):
         n = int(rng.integers(1, 17))
         lens = np.exp(rng.uniform(np.log(8), np.log(513), size=n)).astype(np.int32).clip(8, 512)
         reqs.append((synth.make_ids(lens, cfg.vocab_size, 9000 + i), lens))
-    emb = embedder.Embedder(cfg, synth.make_weights(cfg, 1), devices=range(args.gpus), dtype="bf16")
+    if args.clients <= 0:
+        args.clients = 256 * args.gpus
+    emb = embedder.Embedder(cfg, synth.make_weights(cfg, 1), devices=range(args.gpus), dtype="bf16",
+                            max_tokens=args.max_tokens or None)
     srv = embedder.Server(emb, max_in_flight=16384)
     for r in reqs[:64]:  # warm-up: workspaces, kernels
         srv.submit(*r).result()
@@ -185,7 +188,8 @@ def run_server_mix(args):
         "unit": "vectors/s", "n_gpus": args.gpus, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "cfg5: requests of U{1..16} texts, lengths log-uniform [8,512], <=16384 sequences "
                                "in flight, round-robin over per-GPU replicas",
-                   "requests": args.requests, "clients": args.clients, "vectors": nvec},
+                   "requests": args.requests, "clients": args.clients, "vectors": nvec,
+                   "max_batch": emb.max_batch, "max_tokens": emb.max_tokens},
         "latency_ms": {"p50": float(np.percentile(lat_ms, 50)), "p99": float(np.percentile(lat_ms, 99))},
         "wall_s": wall}), flush=True)
 
@@ -204,7 +208,8 @@ def main():
                     help="N>1: all-gather every step's pooled vectors to all ranks over NCCL inside the timed region")
     ap.add_argument("--lat-iters", type=int, default=50, help="single-request latency samples")
     ap.add_argument("--requests", type=int, default=20000, help="cfg5: requests in the sample")
-    ap.add_argument("--clients", type=int, default=256, help="cfg5: concurrent closed-loop clients")
+    ap.add_argument("--clients", type=int, default=0, help="cfg5: concurrent closed-loop clients (default 256 per GPU)")
+    ap.add_argument("--max-tokens", type=int, default=0, help="cfg5: token budget per device batch (default: by VRAM)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload == "cfg5":

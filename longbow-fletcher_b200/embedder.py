@@ -67,14 +67,21 @@ class Replica:
 
 class Embedder:
     def __init__(self, cfg: synth.BertConfig, blob, devices=None, dtype="bf16", pooling=fletcher.POOL_MEAN_L2,
-                 max_batch=512, max_tokens=16384):
+                 max_batch=512, max_tokens=None):
         n = fletcher.lib().Cuda_GetDeviceCount()
         devices = list(range(n)) if devices is None else list(devices)
         if not devices:
             raise fletcher.FletcherError(-1, "no CUDA device")
         self.cfg = cfg
-        self.max_batch, self.max_tokens = max_batch, max_tokens
         self.replicas = [Replica(d, cfg, blob, dtype, pooling) for d in devices]
+        if max_tokens is None:
+            # The reference's Linux GPU default is 16384 tokens per device batch, "VRAM dependent"
+            # (embeddings.go:177-190).  On devices with 64 GB or more (a B200 has 180 GB) the
+            # budget is 65536 tokens: about 1 GB of workspace, and batches that keep the GEMMs
+            # efficient.
+            total = min(r.be.vram_usage()[1] for r in self.replicas)
+            max_tokens = 65536 if total >= 64 << 30 else 16384
+        self.max_batch, self.max_tokens = max_batch, max_tokens
 
     def embed(self, ids, lengths):
         """Packed ids ([CLS] ... [SEP] per sequence) and lengths -> [B, H] in request order."""
