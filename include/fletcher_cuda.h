@@ -214,6 +214,22 @@ int32_t Cuda_Model_ForwardBatch(CudaModelRef model, const int32_t* ids, const in
  * reference's fp16 transport, Cast(Float16) + ExtractBytes (embeddings.go:256-288). */
 int32_t Cuda_Model_ForwardBatchEx(CudaModelRef model, const int32_t* ids, const int32_t* lengths,
                                   int32_t numSeqs, int32_t pooling, int32_t out_dtype, void* out);
+/* Asynchronous Cuda_Model_ForwardBatchEx for a batcher's double buffering (the reference's
+ * per-device loop, embeddings.go:678-815, waits for each batch before forming the next).  It
+ * enqueues the H2D copy of ids, the pass and the D2H copy of the vectors into `out` on the
+ * context's stream and returns without waiting; *ticket identifies the batch.  lengths are
+ * consumed before the call returns.  ids and out must stay valid until Cuda_Model_Wait(ticket)
+ * returns; with pinned buffers (Cuda_HostAlloc) the copies overlap other batches' compute.  At
+ * most 8 batches are in flight: a ninth call first waits for the oldest. */
+int32_t Cuda_Model_ForwardBatchAsync(CudaModelRef model, const int32_t* ids, const int32_t* lengths,
+                                     int32_t numSeqs, int32_t pooling, int32_t out_dtype, void* out,
+                                     int64_t* ticket);
+/* Waits until batch `ticket` has finished and its vectors are in host memory; reports a
+ * device-side error of any batch up to it. */
+int32_t Cuda_Model_Wait(CudaModelRef model, int64_t ticket);
+/* Page-locked host memory for the asynchronous copies (cudaHostAlloc / cudaFreeHost). */
+void* Cuda_HostAlloc(CudaContextRef ctx, int64_t bytes);
+void Cuda_HostFree(CudaContextRef ctx, void* p);
 /* Same pass with device-resident ids (int32, packed) and a device float32 output; lengths
  * stay on the host (they shape the launch).  Asynchronous on the context's stream. */
 int32_t Cuda_Model_ForwardBatchDevice(CudaModelRef model, const int32_t* d_ids,

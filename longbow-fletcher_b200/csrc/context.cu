@@ -167,6 +167,26 @@ void Cuda_FreeContext(CudaContextRef ctx) {
   delete c;
 }
 
+void* Cuda_HostAlloc(CudaContextRef ctx, int64_t bytes) {
+  Ctx* c = C(ctx);
+  if (!c || bytes <= 0) return nullptr;
+  DeviceGuard g(c);
+  void* p = nullptr;
+  if (cudaHostAlloc(&p, (size_t)bytes, cudaHostAllocPortable) != cudaSuccess) {
+    cudaGetLastError();
+    set_error(c, FLETCHER_ERR_OOM, "cudaHostAlloc of %lld bytes failed", (long long)bytes);
+    return nullptr;
+  }
+  return p;
+}
+
+void Cuda_HostFree(CudaContextRef ctx, void* p) {
+  Ctx* c = C(ctx);
+  if (!p) return;
+  if (c) cudaSetDevice(c->device);
+  cudaFreeHost(p);
+}
+
 int32_t Cuda_GetLastError(CudaContextRef ctx, char* buf, int32_t len) {
   Ctx* c = C(ctx);
   if (!buf || len <= 0) return FLETCHER_ERR_INVALID;

@@ -83,6 +83,10 @@ struct Model {
   // stage timing
   bool timing = false;
   std::vector<cudaEvent_t> ev_pool;
+  // Asynchronous batches (Cuda_Model_ForwardBatchAsync): a completion event per in-flight slot.
+  static constexpr int kAsyncSlots = 8;
+  cudaEvent_t async_ev[kAsyncSlots] = {};
+  int64_t async_issued = 0, async_done = 0;  // tickets issued / known complete
   size_t ev_used = 0;
   struct StageRec {
     int cat;
@@ -610,6 +614,8 @@ static void destroy(Model* m) {
   if (m->h_meta) cudaFreeHost(m->h_meta);
   if (m->meta_done) cudaEventDestroy(m->meta_done);
   for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
+  for (cudaEvent_t e : m->async_ev)
+    if (e) cudaEventDestroy(e);
   delete m;
 }
 
@@ -677,6 +683,63 @@ int32_t Cuda_Model_ForwardBatchEx(CudaModelRef model, const int32_t* ids, const 
   }
   FL_CUDA(c, cudaStreamSynchronize(c->stream));
   return check_device_flag(c);
+}
+
+// Waits for tickets up to `ticket` (slots are reused every kAsyncSlots tickets).
+static int32_t wait_ticket(Model* m, int64_t ticket) {
+  Ctx* c = m->c;
+  FL_CHECK(c, ticket >= 1 && ticket <= m->async_issued, "Wait: unknown ticket %lld", (long long)ticket);
+  if (ticket <= m->async_done) return FLETCHER_OK;
+  FL_CUDA(c, cudaEventSynchronize(m->async_ev[(ticket - 1) % Model::kAsyncSlots]));
+  m->async_done = ticket;
+  return check_device_flag(c);
+}
+
+int32_t Cuda_Model_ForwardBatchAsync(CudaModelRef model, const int32_t* ids, const int32_t* lengths, int32_t B,
+                                     int32_t pooling, int32_t out_dtype, void* out, int64_t* ticket) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m || !ids || !lengths || !out || !ticket) return FLETCHER_ERR_INVALID;
+  Ctx* c = m->c;
+  DeviceGuard g(c);
+  FL_CHECK(c, out_dtype >= FLETCHER_F32 && out_dtype <= FLETCHER_BF16, "ForwardBatchAsync: bad output dtype %d",
+           out_dtype);
+  FL_CHECK(c, B > 0, "ForwardBatch: empty batch");
+  int32_t rc;
+  // A free slot: the ticket issued kAsyncSlots ago must be complete.
+  if (m->async_issued - m->async_done >= Model::kAsyncSlots &&
+      (rc = wait_ticket(m, m->async_issued - Model::kAsyncSlots + 1)))
+    return rc;
+  int64_t T = 0;
+  for (int i = 0; i < B; i++) T += lengths[i] > 0 ? lengths[i] : 0;
+  for (int64_t t = 0; t < T; t++)
+    FL_CHECK(c, ids[t] >= 0 && ids[t] < m->cfg.vocab_size, "Gather index out of bounds: ids[%lld]=%d",
+             (long long)t, ids[t]);
+  // A larger batch reallocates the workspace and drops the captured graphs: let the batches in
+  // flight finish first.
+  if ((T > m->ws_T || B > m->ws_B) && m->async_issued > m->async_done && (rc = wait_ticket(m, m->async_issued)))
+    return rc;
+  if ((rc = ensure_ws(m, T, B))) return rc;
+  FL_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, T * 4, cudaMemcpyHostToDevice, c->stream));
+  if ((rc = forward_device(m, m->d_ids, lengths, B, pooling, m->d_out))) return rc;
+  const int64_t n = (int64_t)B * m->H;
+  if (out_dtype == FLETCHER_F32) {
+    FL_CUDA(c, cudaMemcpyAsync(out, m->d_out, n * 4, cudaMemcpyDeviceToHost, c->stream));
+  } else {
+    if ((rc = launch_cast(c, FLETCHER_F32, m->d_out, out_dtype, m->d_cls, n))) return rc;
+    FL_CUDA(c, cudaMemcpyAsync(out, m->d_cls, n * 2, cudaMemcpyDeviceToHost, c->stream));
+  }
+  const int slot = (int)(m->async_issued % Model::kAsyncSlots);
+  if (!m->async_ev[slot]) FL_CUDA(c, cudaEventCreateWithFlags(&m->async_ev[slot], cudaEventDisableTiming));
+  FL_CUDA(c, cudaEventRecord(m->async_ev[slot], c->stream));
+  *ticket = ++m->async_issued;
+  return FLETCHER_OK;
+}
+
+int32_t Cuda_Model_Wait(CudaModelRef model, int64_t ticket) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(m->c);
+  return wait_ticket(m, ticket);
 }
 
 int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count) {

@@ -2,7 +2,9 @@
 internal/embeddings/embeddings.go).
 
 Embedder.embed: one model replica per GPU, each driven by its own host thread (ctypes releases
-the GIL during library calls, so the replicas run concurrently).  A request is split across
+the GIL during library calls, so the replicas run concurrently).  Each replica keeps two device
+batches in flight (Cuda_Model_ForwardBatchAsync with pinned buffers), so host work overlaps the
+device.  A request is split across
 replicas by token count weighted by each replica's measured throughput (embeddings.go:436-501),
 each replica cuts its share into dynamic batches of at most `max_batch` sequences /
 `max_tokens` tokens (embeddings.go:704-731), and the vectors come back in request order.
@@ -14,6 +16,7 @@ hands batches to the replicas round-robin; every request gets its vectors and it
 """
 from __future__ import annotations
 
+import collections
 import concurrent.futures as cf
 import queue
 import threading
@@ -26,43 +29,134 @@ import replicas
 import synth
 
 
+class _Job:
+    """One run() call: its device batches, output rows and future."""
+
+    def __init__(self, ids, lengths, max_batch, max_tokens, hidden):
+        self.ids, self.lengths = ids, lengths
+        self.cu = np.concatenate([[0], np.cumsum(lengths)])
+        self.todo = collections.deque(replicas.dynamic_batches(lengths, max_batch, max_tokens))
+        self.pending = len(self.todo)  # device batches not yet collected
+        self.out = np.zeros((len(lengths), hidden), np.float32)
+        self.error = None
+        self.future = cf.Future()
+        self.t0 = time.perf_counter()
+
+
 class Replica:
-    """One GPU: its own context, model and worker thread."""
+    """One GPU: its own context, model and worker thread.
+
+    The worker keeps two device batches in flight (Cuda_Model_ForwardBatchAsync with pinned
+    ids and vectors): while the device runs batch k+1, the host stages the next batch and
+    collects batch k, across run() calls as well as within one.  run() returns a future."""
 
     def __init__(self, device, cfg, blob, dtype, pooling):
-        self.pool = cf.ThreadPoolExecutor(max_workers=1)
         self.device = device
         self.pooling = pooling
         self.throughput = 0.0  # sequences/s, exponential moving average (embeddings.go GPUMetrics)
+        self.slots = [(None, None), (None, None)]  # pinned ids / vectors of the two in-flight batches
+        self.jobs = queue.Queue()
+        ready = cf.Future()
+        self.thread = threading.Thread(target=self._loop, args=(cfg, blob, dtype, ready), daemon=True)
+        self.thread.start()
+        ready.result()
 
-        def init():
-            self.be = fletcher.Backend(device, dtype)
+    def _slot(self, k, n_ids, n_seq):
+        """Pinned staging buffers of in-flight slot k (grown when a batch does not fit)."""
+        ids_buf, out_buf = self.slots[k]
+        if ids_buf is None or ids_buf.array.size < n_ids:
+            if ids_buf is not None:
+                ids_buf.close()
+            ids_buf = fletcher.PinnedArray(self.be, (max(n_ids, 1 << 14),), np.int32)
+        if out_buf is None or out_buf.array.shape[0] < n_seq:
+            if out_buf is not None:
+                out_buf.close()
+            out_buf = fletcher.PinnedArray(self.be, (max(n_seq, 64), self.model.cfg.hidden), np.float32)
+        self.slots[k] = (ids_buf, out_buf)
+        return ids_buf, out_buf
+
+    def _finish(self, job):
+        if job.error is not None:
+            job.future.set_exception(job.error)
+            return
+        dt = time.perf_counter() - job.t0
+        if dt > 0 and len(job.lengths):
+            r = len(job.lengths) / dt
+            self.throughput = r if self.throughput == 0 else 0.8 * self.throughput + 0.2 * r
+        job.future.set_result(job.out)
+
+    def _loop(self, cfg, blob, dtype, ready):
+        try:
+            self.be = fletcher.Backend(self.device, dtype)
             self.model = fletcher.BertModel(self.be, cfg, dtype)
             self.model.load_raw(blob)
-
-        self.pool.submit(init).result()
+        except Exception as e:  # noqa: BLE001 - reported to the constructor
+            ready.set_exception(e)
+            return
+        ready.set_result(None)
+        todo = collections.deque()      # jobs with device batches left to enqueue
+        inflight = collections.deque()  # (ticket, slot, job, a, b)
+        nslot = 0
+        stop = False
+        while not stop or todo or inflight:
+            if not stop:
+                try:
+                    job = self.jobs.get(block=not (todo or inflight))
+                    if job is None:
+                        stop = True
+                    else:
+                        todo.append(job)
+                    continue
+                except queue.Empty:
+                    pass
+            if todo and len(inflight) < len(self.slots):
+                job = todo[0]
+                a, b = job.todo.popleft()
+                if not job.todo:
+                    todo.popleft()
+                k = nslot % len(self.slots)  # FIFO collection frees slots in this order
+                nslot += 1
+                ticket = None
+                if job.error is None:
+                    try:
+                        ids_buf, out_buf = self._slot(k, int(job.cu[b] - job.cu[a]), b - a)
+                        ids_buf.array[:job.cu[b] - job.cu[a]] = job.ids[job.cu[a]:job.cu[b]]
+                        ticket = self.model.forward_batch_async(ids_buf.ptr, job.lengths[a:b], self.pooling,
+                                                                out_buf.ptr)
+                    except Exception as e:  # noqa: BLE001 - the reference fails the whole request
+                        job.error = e
+                inflight.append((ticket, k, job, a, b))
+            elif inflight:
+                ticket, k, job, a, b = inflight.popleft()
+                if ticket is not None:
+                    try:
+                        self.model.wait(ticket)
+                        if job.error is None:
+                            job.out[a:b] = self.slots[k][1].array[:b - a]
+                    except Exception as e:  # noqa: BLE001
+                        job.error = e
+                job.pending -= 1
+                if job.pending == 0:
+                    self._finish(job)
+        for bufs in self.slots:
+            for buf in bufs:
+                if buf is not None:
+                    buf.close()
+        self.model.close()
+        self.be.close()
 
     def run(self, ids, lengths, max_batch, max_tokens):
-        """Embeds packed (ids, lengths) in dynamic batches; returns [B, H] float32."""
-        def work():
-            t0 = time.perf_counter()
-            out = []
-            cu = np.concatenate([[0], np.cumsum(lengths)])
-            for a, b in replicas.dynamic_batches(lengths, max_batch, max_tokens):
-                out.append(self.model.forward_batch(ids[cu[a]:cu[b]], lengths[a:b], self.pooling))
-            dt = time.perf_counter() - t0
-            if dt > 0 and len(lengths):
-                r = len(lengths) / dt
-                self.throughput = r if self.throughput == 0 else 0.8 * self.throughput + 0.2 * r
-            return np.concatenate(out) if out else np.zeros((0, self.model.cfg.hidden), np.float32)
-        return self.pool.submit(work)
+        """Embeds packed (ids, lengths) in dynamic batches; a future of [B, H] float32."""
+        job = _Job(ids, np.asarray(lengths), max_batch, max_tokens, self.model.cfg.hidden)
+        if job.pending == 0:
+            job.future.set_result(job.out)
+        else:
+            self.jobs.put(job)
+        return job.future
 
     def close(self):
-        def fin():
-            self.model.close()
-            self.be.close()
-        self.pool.submit(fin).result()
-        self.pool.shutdown()
+        self.jobs.put(None)
+        self.thread.join()
 
 
 class Embedder:

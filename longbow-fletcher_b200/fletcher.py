@@ -83,6 +83,10 @@ def _sig(L):
         "Cuda_Model_ForwardBatch": (i32, [vp, i32p, i32p, i32, i32, f32p]),
         "Cuda_Model_ForwardBatchDevice": (i32, [vp, vp, i32p, i32, i32, vp]),
         "Cuda_Model_ForwardBatchEx": (i32, [vp, i32p, i32p, i32, i32, i32, vp]),
+        "Cuda_Model_ForwardBatchAsync": (i32, [vp, vp, i32p, i32, i32, i32, vp, i64p]),
+        "Cuda_Model_Wait": (i32, [vp, i64]),
+        "Cuda_HostAlloc": (vp, [vp, i64]),
+        "Cuda_HostFree": (None, [vp, vp]),
         "Cuda_Model_LastHidden": (i32, [vp, f32p, i64]),
         "Cuda_Model_SetStageTiming": (i32, [vp, i32]),
         "Cuda_Model_SetGraphs": (i32, [vp, i32]),
@@ -113,6 +117,26 @@ def _i32p(a):
 
 def _f32p(a):
     return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+class PinnedArray:
+    """Page-locked host array (Cuda_HostAlloc) viewed as numpy; freed with close()."""
+
+    def __init__(self, be, shape, dtype):
+        self.be = be
+        self.dtype = np.dtype(dtype)
+        n = int(np.prod(shape)) * self.dtype.itemsize
+        self.ptr = lib().Cuda_HostAlloc(be.ctx, max(n, 1))
+        if not self.ptr:
+            be.check(3)  # FLETCHER_ERR_OOM
+        buf = (ctypes.c_uint8 * max(n, 1)).from_address(self.ptr)
+        self.array = np.frombuffer(buf, dtype=self.dtype, count=int(np.prod(shape))).reshape(shape)
+
+    def close(self):
+        if self.ptr:
+            self.array = None
+            lib().Cuda_HostFree(self.be.ctx, self.ptr)
+            self.ptr = None
 
 
 class Backend:
@@ -317,6 +341,19 @@ class BertModel:
         self.be.check(lib().Cuda_Model_ForwardBatchEx(self.h, _i32p(ids), _i32p(lens), lens.size, pooling, out_dtype,
                                                       out.ctypes.data))
         return out
+
+    def forward_batch_async(self, ids_ptr, lengths, pooling, out_ptr, out_dtype=F32):
+        """Enqueues a batch (ids and out: host pointers that stay valid until wait(ticket));
+        returns its ticket.  The double-buffering half of the batcher loop."""
+        lens = np.ascontiguousarray(lengths, np.int32)
+        t = ctypes.c_int64()
+        self.be.check(lib().Cuda_Model_ForwardBatchAsync(self.h, ctypes.c_void_p(ids_ptr), _i32p(lens), lens.size,
+                                                         pooling, out_dtype, ctypes.c_void_p(out_ptr),
+                                                         ctypes.byref(t)))
+        return t.value
+
+    def wait(self, ticket):
+        self.be.check(lib().Cuda_Model_Wait(self.h, ticket))
 
     def forward_batch_device(self, d_ids_ptr, lengths, pooling, d_out_ptr):
         lens = np.ascontiguousarray(lengths, np.int32)

@@ -183,3 +183,28 @@ def test_safetensors_checkpoint_end_to_end(be, tmp_path, oracle_mod):
     want = oracle_mod.forward(cfg, loaded, ids, lens)["mean"]
     assert_close_16(m.forward_batch(ids, lens, 1), want, "safetensors bf16")
     m.close()
+
+
+def test_async_batches_match_sync(be):
+    """Cuda_Model_ForwardBatchAsync / Cuda_Model_Wait: several batches in flight (more than the
+    eight slots), pinned buffers, waits in any order; the vectors equal the synchronous call's."""
+    import fletcher
+    cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
+    m = model(be, cfg, "bf16", 1)
+    batches = []
+    for i, lengths in enumerate([[40, 7, 300], [129, 64], [512], [5, 5, 5, 5]] * 3):
+        lens = np.array(lengths, np.int32)
+        batches.append((synth.make_ids(lens, cfg.vocab_size, 40 + i), lens))
+    want = [m.forward_batch(ids, lens, 1) for ids, lens in batches]
+    bufs = [(fletcher.PinnedArray(be, (ids.size,), np.int32), fletcher.PinnedArray(be, (lens.size, cfg.hidden), np.float32))
+            for ids, lens in batches]
+    tickets = []
+    for (ids, lens), (bi, bo) in zip(batches, bufs):
+        bi.array[:] = ids
+        tickets.append(m.forward_batch_async(bi.ptr, lens, 1, bo.ptr))
+    for t in reversed(tickets):
+        m.wait(t)
+    for w, (bi, bo) in zip(want, bufs):
+        assert np.array_equal(bo.array, w)
+        bi.close()
+        bo.close()
