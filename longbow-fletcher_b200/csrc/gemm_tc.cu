@@ -40,23 +40,26 @@ constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;            // + producer warp + MMA warp
 constexpr int kStageOut = 32 * 128;                    // per-warp output box: 32 rows x 64 cols x 2 B
-constexpr int kOutBufs = 2;                            // output boxes in flight per warp
 // Epilogues drained by alternating warp groups (see the epilogue section of k_gemm_tc).
 template <int EPI>
 constexpr bool kEpiGroups = EPI == 0 || EPI == 1 || EPI == 2 || EPI == 5;  // STORE, ROPE, GELU, PARTIAL
+// Output boxes in flight per warp: two where a warp writes four boxes per tile (the groups),
+// one for the residual and SwiGLU epilogues, whose shared memory goes to an extra operand stage.
+template <int EPI>
+constexpr int kOutBufs = kEpiGroups<EPI> ? 2 : 1;
 
 // PAIR: the tile is computed by a cluster of two CTAs on two SMs with tcgen05 cta_group::2
 // (M = 256 per MMA): each CTA loads its 128 rows of A and half of the tile's BN rows of W, and
 // holds its 128 rows of the accumulator.  Per SM that is a third less operand traffic than a
 // 128 x 256 tile on one SM.
-template <int BN, bool PAIR>
+template <int BN, bool PAIR, int OUT_BUFS>
 struct Cfg {
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of W loaded by one CTA
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;  // rows of a tile
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int OUT_BYTES = kEpiWarps * kOutBufs * kStageOut;
+  static constexpr int OUT_BYTES = kEpiWarps * OUT_BUFS * kStageOut;
   // As many operand stages as fit next to the output staging (at most 8).
   static constexpr int STAGES_FIT = (232448 - 1024 - 256 - OUT_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT < 8 ? STAGES_FIT : 8;
@@ -108,7 +111,7 @@ template <typename T, int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
-  using C = Cfg<BN, PAIR>;
+  using C = Cfg<BN, PAIR, kOutBufs<EPI>>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -264,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int grp = GROUPS ? (warp - 2) >> 2 : 0;
     const int col0 = GROUPS ? 0 : ((warp - 2) >> 2) * (EPI == EPI_SWIGLU ? 64 : BN / 2);
-    uint8_t* stg0 = smem + C::OUT_OFF + (warp - 2) * kOutBufs * kStageOut;
+    uint8_t* stg0 = smem + C::OUT_OFF + (warp - 2) * kOutBufs<EPI> * kStageOut;
     int ob = 0;  // output buffer of the next box
     // 64-column output units per warp: SwiGLU halves the width (BN/2 outputs per tile).
     constexpr int UNITS = (EPI == EPI_SWIGLU ? BN / 128 : BN / 64) / (GROUPS ? 1 : 2);
@@ -418,7 +421,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else if (ocol < n_out && row0 < args.M) {
           uint8_t* stg = stg0 + ob * kStageOut;
-          if (lane == 0) bulk_wait_read1();  // the box stored from this buffer has left it
+          if (lane == 0) {  // the box stored from this buffer has left it
+            if constexpr (kOutBufs<EPI> == 2)
+              bulk_wait_read1();
+            else
+              bulk_wait_read0();
+          }
           __syncwarp();
           stage_row<T>(stg, lane, a, b);
           fence_async_smem();
@@ -427,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_store_2d(&tmC, stg, (int)ocol, row0);  // rows >= M are clipped by TMA
             bulk_commit();
           }
-          ob ^= 1;
+          ob = (ob + 1) % kOutBufs<EPI>;
         }
       }
     }
@@ -568,7 +576,7 @@ static int32_t make_map(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, 
 
 template <typename T, int BN, int EPI, bool PAIR>
 static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmArgs a) {
-  using Cf = Cfg<BN, PAIR>;
+  using Cf = Cfg<BN, PAIR, kOutBufs<EPI>>;
   auto kern = k_gemm_tc<T, BN, EPI, PAIR>;
   static bool attr_set[64] = {};  // per device
   if (!attr_set[c->device & 63]) {
