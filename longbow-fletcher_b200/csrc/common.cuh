@@ -135,6 +135,16 @@ __device__ __forceinline__ float gelu_fast(float x) {
   float th = tanh_fast(__fmul_rn(0.7978846f, __fadd_rn(x, c3)));
   return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, th));
 }
+// GeluFast for the 16-bit epilogues: the same formula with fused multiply-adds and a fast
+// division (a few ulp of fp32, far below the 16-bit output's resolution), as selects rather than
+// branches.
+__device__ __forceinline__ float gelu_fast16(float x) {
+  const float u = 0.7978846f * fmaf(0.044715f * x, x * x, x);
+  const float u2 = u * u;
+  const float pade = __fdividef(u * (27.0f + u2), fmaf(9.0f, u2, 27.0f));
+  const float th = fabsf(u) > 4.0f ? copysignf(1.0f, u) : pade;
+  return 0.5f * x * (1.0f + th);
+}
 // SwiGLU element (cpu_backend.go:649-650): x / (1 + float32(exp(float64(-x)))) * y.
 __device__ __forceinline__ float swiglu_exact(float x, float y) {
   float e = (float)exp(-(double)x);

@@ -386,8 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (EPI == EPI_GELU) {
 #pragma unroll
               for (int i = 0; i < 32; i++) {
-                a[i] = gelu_fast(a[i]);
-                b[i] = gelu_fast(b[i]);
+                a[i] = gelu_fast16(a[i]);
+                b[i] = gelu_fast16(b[i]);
               }
             }
             if constexpr (EPI == EPI_RESIDUAL) {
@@ -530,8 +530,8 @@ __global__ void __launch_bounds__(256)
         out[row * ld_out + o1] = from_f<T>(b);
       } else {
         if constexpr (EPI == EPI_GELU) {
-          a = gelu_fast(a);
-          b = gelu_fast(b);
+          a = gelu_fast16(a);
+          b = gelu_fast16(b);
         }
         if constexpr (EPI == EPI_RESIDUAL) {
           a += to_f<T>(res[row * ld_res + o0]);
