@@ -39,8 +39,8 @@ import synth  # noqa: E402
 
 METRIC = "embeddings/sec (nomic-embed-text seq512 bf16)"
 # ncu-measured DRAM traffic (read + write) of the four tensor-core GEMMs of one nomic layer, per
-# token (profiles/gemm_tc_cfg3.md: 1687 MB for 65.6K tokens).  Scaled to the timed forwards.
-GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 25733.0
+# token (profiles/gemm_tc_cfg3.md: 1680 MB for 65.6K tokens).  Scaled to the timed forwards.
+GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 25625.0
 
 
 def peaks():
