@@ -432,7 +432,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, stg, (int)ocol, row0);  // rows >= M are clipped by TMA
+            // rows >= M are clipped by TMA; the residual sum is kept in L2 for the LayerNorm after it
+            if constexpr (EPI == EPI_RESIDUAL)
+              tma_store_2d_keep(&tmC, stg, (int)ocol, row0);
+            else
+              tma_store_2d(&tmC, stg, (int)ocol, row0);
             bulk_commit();
           }
           ob = (ob + 1) % kOutBufs<EPI>;

@@ -128,6 +128,15 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// TMA store whose lines L2 keeps preferentially (evict-last policy): for outputs that the next
+// kernel reads right away.
+__device__ __forceinline__ void tma_store_2d_keep(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile(
+      "{\n .reg .b64 pol;\n createpolicy.fractional.L2::evict_last.b64 pol, 1.0;\n"
+      " cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], pol;\n}" ::"l"(map),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
