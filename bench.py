@@ -316,9 +316,7 @@ def main():
                                 "per-token figure scaled to the timed forwards",
                 # activations in + out of the 4 GEMMs: reads 5H + I, writes 5H + I per token (16-bit)
                 "algorithmic_bytes_per_launch": 2.0 * tok_ns * L * (10 * Hh + 2 * I) / gemm_launches,
-                "flops_per_launch": gemm_flops / gemm_launches, "ms_per_launch": gemm_ms / gemm_launches,
-                "note": "the attention-output and FFN-down GEMMs include the LayerNorm fused into their "
-                        "epilogue (hidden 768); their time counts in the GEMM time"}
+                "flops_per_launch": gemm_flops / gemm_launches, "ms_per_launch": gemm_ms / gemm_launches}
     stage_ms = {k: v[0] / ns for k, v in st.items() if v[1]}
     # HBM-bound kernels: algorithmic bytes of the stage-timing forwards / their event time.
     es = 4 if w.dtype == "f32" else 2

@@ -162,44 +162,4 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-template <typename T, int VEC>
-struct alignas(sizeof(T) * VEC) Vec {
-  T d[VEC];
-};
-
-// ---------------------------------------------------------------- LayerNorm core
-// Two-pass statistics over the row held in registers (cpu_backend.go:579-600):
-// mean = sum/c, var = sum((x-mean)^2)/c, invStd = 1/float32(sqrt(float64(var+eps))),
-// y = (x-mean)*invStd*gamma + beta.  Sums are warp-tree reductions (order differs from the
-// reference's sequential sum by rounding only).
-template <typename T, int PER, int VEC>
-__device__ __forceinline__ void ln_finish(float (&v)[PER], int lane, int cols, const float* __restrict__ g,
-                                          const float* __restrict__ b, float eps, T* __restrict__ orow) {
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < PER; i++) s += v[i];
-  s = warp_sum(s);
-  const float mean = __fdiv_rn(s, (float)cols);
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < PER; i++) {
-    float d = __fsub_rn(v[i], mean);
-    q = __fadd_rn(q, __fmul_rn(d, d));
-  }
-  q = warp_sum(q);
-  const float var = __fdiv_rn(q, (float)cols);
-  const float inv = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(var, eps)));
-#pragma unroll
-  for (int j = 0; j < PER / VEC; j++) {
-    const int e = (j * 32 + lane) * VEC;
-    Vec<float, VEC> gv = *reinterpret_cast<const Vec<float, VEC>*>(g + e);
-    Vec<float, VEC> bv = *reinterpret_cast<const Vec<float, VEC>*>(b + e);
-    Vec<T, VEC> o;
-#pragma unroll
-    for (int i = 0; i < VEC; i++)
-      o.d[i] = from_f<T>(__fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j * VEC + i], mean), inv), gv.d[i]), bv.d[i]));
-    *reinterpret_cast<Vec<T, VEC>*>(orow + e) = o;
-  }
-}
-
 }  // namespace fl

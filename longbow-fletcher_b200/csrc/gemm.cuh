@@ -31,14 +31,6 @@ struct GemmArgs {
   int splits;      // K ranges per output tile (1 unless EPI_PARTIAL)
   int kb_per;      // 64-wide K blocks per range
   float* partial;  // EPI_PARTIAL: [splits, M, N] fp32
-  // Residual + LayerNorm (EPI_RESIDUAL with ln_cnt set, N = 768): once every tile of a 128-row
-  // block of `out` is stored, the CTA that stored the last one writes ln_out = LayerNorm(out)
-  // for those rows.  ln_cnt[block] counts the stored tiles and is zero between launches.
-  int32_t* ln_cnt;
-  void* ln_out;
-  const float* ln_g;
-  const float* ln_b;
-  float ln_eps;
 };
 
 bool gemm_tc_supported(int64_t M, int64_t N, int64_t K, int bn);
@@ -52,14 +44,6 @@ int64_t gemm_splitk_plan(const Ctx* c, int64_t M, int64_t N, int64_t K, int* spl
 int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, int64_t M, int64_t K, const void* W,
                        int64_t N, void* out, int64_t ld_out, const float* bias, const void* residual, int64_t ld_res,
                        const int32_t* pos, const float* cos_t, const float* sin_t, int64_t rope_cols);
-
-// S = A . W^T + bias + X, then X = LayerNorm(S) with gamma g, beta b (rows of N = hidden
-// columns).  With ln_cnt (ceil(M / 128) + 2 zeroed ints owned by the caller) and a shape the
-// fused epilogue supports (no split-K, N = 768), the LayerNorm runs in the GEMM's epilogue;
-// otherwise as its own kernel.  *fused reports which (may be null).
-int32_t launch_gemm_residual_ln(Ctx* c, int32_t dtype, int bn, const void* A, int64_t M, int64_t K, const void* W,
-                                int64_t N, void* S, const float* bias, void* X, const float* g, const float* b,
-                                float eps, int32_t* ln_cnt, bool* fused);
 
 // SIMT GEMM for any dtype (fp32 compute): C[M,N] = act(A[M,K] . B[K,N] + bias) with B row-major
 // (in, out) and optional row gather of A.  Used for fp32 parity mode and small/odd shapes.

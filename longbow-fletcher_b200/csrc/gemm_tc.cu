@@ -68,7 +68,6 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM = BAR_OFF + 256 /*barriers*/ + 1024 /*alignment slack*/;
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert((2 * STAGES + 7) * 8 <= 256, "barrier area");
 };
 
 
@@ -108,43 +107,6 @@ __device__ __forceinline__ void add_packed(float (&v)[32], const uint4* q4) {
   }
 }
 
-// Residual + LayerNorm: X = LayerNorm(S) over rows [r0, r0 + 128) of the residual GEMM's output
-// S (rows of NJ * 256 columns), once every tile of those rows has been stored (by this CTA or
-// others, so S is read through L2).  Epilogue warp w (0-7) takes rows w, w + 8, ...; ln_finish
-// is the LayerNorm kernel's arithmetic, so the results are identical to it.
-template <typename T, int NJ>
-__device__ __forceinline__ void ln_block(const T* __restrict__ S, T* __restrict__ X, int64_t M, const float* g,
-                                         const float* b, float eps, int64_t r0, int w, int lane) {
-  // R rows' loads in flight, held packed (NJ 16-byte words per row and lane) until their turn.
-  constexpr int PER = NJ * 8, R = 2, H = NJ * 256;
-  for (int rr = w; rr < BM; rr += kEpiWarps * R) {
-    uint4 pk[R][NJ];
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-      const int64_t row = r0 + rr + r * kEpiWarps;
-      if (row < M) {
-#pragma unroll
-        for (int j = 0; j < NJ; j++)
-          pk[r][j] = __ldcg(reinterpret_cast<const uint4*>(S + row * H + (j * 32 + lane) * 8));
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-      const int64_t row = r0 + rr + r * kEpiWarps;
-      if (row < M) {
-        float v[PER];
-#pragma unroll
-        for (int j = 0; j < NJ; j++) {
-          const Vec<T, 8> t = *reinterpret_cast<const Vec<T, 8>*>(&pk[r][j]);
-#pragma unroll
-          for (int i = 0; i < 8; i++) v[j * 8 + i] = to_f<T>(t.d[i]);
-        }
-        ln_finish<T, PER, 8>(v, lane, H, g, b, eps, X + row * H);
-      }
-    }
-  }
-}
-
 template <typename T, int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -162,9 +124,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = bars + 2 * C::STAGES + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  int* ln_arrivals = reinterpret_cast<int*>(tmem_holder + 2);  // epilogue warps done with a tile's stores
-  volatile int* ln_take = reinterpret_cast<volatile int*>(tmem_holder + 3);  // this CTA normalises the block
-  uint64_t* lnbar = bars + 2 * C::STAGES + 6;                                // the decision is published
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = args.num_n_tiles;
@@ -191,8 +150,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[i], (kEpiGroups<EPI> ? kEpiWarps / 2 : kEpiWarps) * (PAIR ? 2 : 1));
     }
     *abort = 0;
-    *ln_arrivals = 0;
-    mbar_init(lnbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0 && lane == 0) {
@@ -320,50 +277,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0;
     auto tile_row = [&](int t) -> int64_t {
       return (int64_t)(t / splits / n_tiles) * C::TILE_M + (int)crank * BM + q * 32 + lane;
-    };
-    // Residual + LayerNorm: after a tile's stores have completed, each epilogue warp counts
-    // itself in; the last of the eight adds the tile to its 128-row block's counter in global
-    // memory, and the CTA whose tile completes the block (all n_tiles column tiles stored, by any
-    // CTAs) normalises it.  Nothing waits for another CTA.  A tile is counted at the end of the
-    // next one, so that its stores have drained meanwhile.
-    auto ln_step = [&](int t, int keep, uint32_t phase) -> bool {
-      const int blk = t / n_tiles * (C::TILE_M / BM) + (int)crank;
-      if (lane == 0) {
-        // At most `keep` (the later tile's) store groups still pending: tile t's are done.
-        if (keep >= 2)
-          bulk_wait2();
-        else if (keep == 1)
-          bulk_wait1();
-        else
-          bulk_wait0();
-        fence_async_global();
-        __threadfence();
-        if (atomicAdd(ln_arrivals, 1) == kEpiWarps - 1) {
-          *ln_arrivals = 0;
-          __threadfence();
-          int32_t* cnt = args.ln_cnt + blk;
-          const int take = atomicAdd(cnt, 1) == n_tiles - 1;
-          if (take) *cnt = 0;  // zero again for the next launch
-          __threadfence();
-          *ln_take = take;
-          mbar_arrive(lnbar);
-        }
-      }
-      __syncwarp();
-      if (!mbar_wait_spin(lnbar, phase, abort, args.err)) return false;
-      if (*ln_take)
-        ln_block<T, 3>(reinterpret_cast<const T*>(args.out), reinterpret_cast<T*>(args.ln_out), args.M, args.ln_g,
-                       args.ln_b, args.ln_eps, (int64_t)blk * BM, warp - 2, lane);
-      return true;
-    };
-    // Output boxes (bulk groups) this warp stores for tile t.
-    auto boxes = [&](int t) -> int {
-      const int64_t r = (int64_t)(t / n_tiles) * C::TILE_M + (int)crank * BM + q * 32;
-      if (r >= args.M) return 0;
-      int n = 0;
-#pragma unroll
-      for (int u = 0; u < UNITS; u++) n += (int64_t)(t % n_tiles) * BN + col0 + u * 64 < n_out;
-      return n;
     };
     // RoPE positions run one tile ahead, so a tile's table loads need no dependent load.
     const int t0 = first_tile + grp * tile_stride;
@@ -519,9 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            // rows >= M are clipped by TMA; without the fused LayerNorm, the residual sum is kept
-            // in L2 for the LayerNorm kernel after it
-            if (EPI == EPI_RESIDUAL && !args.ln_cnt)
+            // rows >= M are clipped by TMA; the residual sum is kept in L2 for the LayerNorm after it
+            if constexpr (EPI == EPI_RESIDUAL)
               tma_store_2d_keep(&tmC, stg, (int)ocol, row0);
             else
               tma_store_2d(&tmC, stg, (int)ocol, row0);
@@ -530,15 +442,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           ob = (ob + 1) % kOutBufs<EPI>;
         }
       }
-      if constexpr (EPI == EPI_RESIDUAL) {  // count the previous tile (`it` tiles drained before this one)
-        if (args.ln_cnt && it > 0 && !ln_step(tile - tile_stride, boxes(tile), (uint32_t)(it - 1) & 1)) break;
-      }
     }
     if (lane == 0) bulk_wait0();
-    if constexpr (EPI == EPI_RESIDUAL) {
-      // `it` is the number of tiles drained (the loop ran to its end unless aborting).
-      if (args.ln_cnt && it > 0 && !*abort) ln_step(t0 + (it - 1) * tile_stride, 0, (uint32_t)(it - 1) & 1);
-    }
   }
 
   tc_fence_before();
@@ -824,29 +729,9 @@ bool gemm_tc_supported(int64_t M, int64_t N, int64_t K, int bn) {
   return M > 0 && M < (1ll << 31) && K % tc::BK == 0 && K > 0 && N % 64 == 0 && (bn == 128 || bn == 256);
 }
 
-// The LayerNorm fused into the residual GEMM (FLETCHER_FUSE_LN=0 runs it as its own kernel, for
-// A/B measurement).
-static bool gemm_ln_fuse_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("FLETCHER_FUSE_LN");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
-
-struct LnFuse {
-  int32_t* cnt;
-  void* out;
-  const float* g;
-  const float* b;
-  float eps;
-};
-
-static int32_t gemm_tc_impl(Ctx* c, int32_t dtype, int epi, int bn, const void* A, int64_t M, int64_t K,
-                            const void* W, int64_t N, void* out, int64_t ld_out, const float* bias,
-                            const void* residual, int64_t ld_res, const int32_t* pos, const float* cos_t,
-                            const float* sin_t, int64_t rope_cols, const LnFuse* ln, bool* fused) {
-  if (fused) *fused = false;
+int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, int64_t M, int64_t K, const void* W,
+                       int64_t N, void* out, int64_t ld_out, const float* bias, const void* residual, int64_t ld_res,
+                       const int32_t* pos, const float* cos_t, const float* sin_t, int64_t rope_cols) {
   FL_CHECK(c, dtype == FLETCHER_BF16 || dtype == FLETCHER_F16, "gemm_tc: 16-bit dtypes only");
   FL_CHECK(c, gemm_tc_supported(M, N, K, bn), "gemm_tc: unsupported shape M=%lld N=%lld K=%lld BN=%d",
            (long long)M, (long long)N, (long long)K, bn);
@@ -890,42 +775,12 @@ static int32_t gemm_tc_impl(Ctx* c, int32_t dtype, int epi, int bn, const void* 
   a.err = c->d_err;
   a.splits = 1;
   a.kb_per = (int)(K / tc::BK);
-  if (ln) {
-    a.ln_cnt = ln->cnt;
-    a.ln_out = ln->out;
-    a.ln_g = ln->g;
-    a.ln_b = ln->b;
-    a.ln_eps = ln->eps;
-    if (fused) *fused = true;
-  }
   if (pair) {
     if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16, true>(c, epi, bn, ma, mb, mc, a);
     return tc::dispatch<__half, true>(c, epi, bn, ma, mb, mc, a);
   }
   if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16, false>(c, epi, bn, ma, mb, mc, a);
   return tc::dispatch<__half, false>(c, epi, bn, ma, mb, mc, a);
-}
-
-int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, int64_t M, int64_t K, const void* W,
-                       int64_t N, void* out, int64_t ld_out, const float* bias, const void* residual, int64_t ld_res,
-                       const int32_t* pos, const float* cos_t, const float* sin_t, int64_t rope_cols) {
-  return gemm_tc_impl(c, dtype, epi, bn, A, M, K, W, N, out, ld_out, bias, residual, ld_res, pos, cos_t, sin_t,
-                      rope_cols, nullptr, nullptr);
-}
-
-int32_t launch_gemm_residual_ln(Ctx* c, int32_t dtype, int bn, const void* A, int64_t M, int64_t K, const void* W,
-                                int64_t N, void* S, const float* bias, void* X, const float* g, const float* b,
-                                float eps, int32_t* ln_cnt, bool* fused) {
-  const bool can = ln_cnt && gemm_ln_fuse_enabled() && N == 768 && ((uintptr_t)X & 15) == 0 &&
-                   ((uintptr_t)g & 31) == 0 && ((uintptr_t)b & 31) == 0;
-  const LnFuse ln{ln_cnt, X, g, b, eps};
-  bool f = false;
-  int32_t rc = gemm_tc_impl(c, dtype, EPI_RESIDUAL, bn, A, M, K, W, N, S, N, bias, X, N, nullptr, nullptr, nullptr, 0,
-                            can ? &ln : nullptr, &f);
-  if (rc) return rc;
-  if (fused) *fused = f;
-  if (f) return FLETCHER_OK;
-  return launch_add_layernorm(c, dtype, S, nullptr, X, g, b, M, N, eps);
 }
 
 }  // namespace fl

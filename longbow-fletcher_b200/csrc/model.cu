@@ -1,16 +1,14 @@
 // Whole-model forward on the device: BertModel.ForwardBatch (bert.go:149-169) with fused
 // kernels, behind Cuda_Model_* of include/fletcher_cuda.h.
 //
-// Per layer (16-bit mode), 5 launches:
+// Per layer (16-bit mode), 7 launches:
 //   QKV   = X . Wqkv^T (+b), RoPE on Q|K in the epilogue          (tcgen05 GEMM, EPI_ROPE)
 //   CTX   = flash-attention(QKV) over packed sequences            (tcgen05 attention)
 //   S     = CTX . Wo^T + bo + X                                   (tcgen05 GEMM, EPI_RESIDUAL)
-//   X     = LayerNorm(S)                                          (in that GEMM's epilogue)
+//   X     = LayerNorm(S)                                          (warp-per-row LN)
 //   ACT   = SwiGLU / GeluFast(X . Wi^T + bi)                      (tcgen05 GEMM, EPI_SWIGLU/GELU)
 //   S     = ACT . Wd^T + bd + X                                   (tcgen05 GEMM, EPI_RESIDUAL)
-//   X     = LayerNorm(S)                                          (in that GEMM's epilogue)
-// The LayerNorms run as their own kernel where the epilogue cannot take them (hidden size other
-// than 768, split-K GEMMs of small batches).
+//   X     = LayerNorm(S)
 // fp32 mode runs the same graph with the SIMT GEMM, a RoPE kernel and the fp32 attention
 // kernel, using the reference's fast-math formulas, for parity with its CPU path.
 // The residual stream X stays in the model dtype; LayerNorm statistics are fp32.  The kernel
@@ -65,7 +63,6 @@ struct Model {
   float* d_cls = nullptr;
   float* splitk = nullptr;  // split-K partial sums of the GEMMs of small batches
   int64_t splitk_bytes = 0;
-  int32_t* ln_cnt = nullptr;  // per 128-row block: tiles stored by the residual GEMM (LayerNorm fusion)
   std::vector<std::pair<void*, int64_t>> ws;
   // pinned staging for per-batch metadata
   uint8_t* h_meta = nullptr;
@@ -158,12 +155,6 @@ static int32_t ensure_ws(Model* m, int64_t T, int32_t B) {
       if ((rc = ws_alloc(m, (void**)&m->splitk, need))) return rc;
       m->splitk_bytes = need;
     }
-  }
-  m->ln_cnt = nullptr;
-  if (m->dtype != FLETCHER_F32) {
-    const int64_t n = Tc / 128 + 2;
-    if ((rc = ws_alloc(m, (void**)&m->ln_cnt, n * 4))) return rc;
-    FL_CUDA(m->c, cudaMemsetAsync(m->ln_cnt, 0, n * 4, m->c->stream));  // the kernels leave them zero
   }
   m->ws_T = Tc;
   m->ws_B = (int32_t)Bc;
@@ -489,12 +480,14 @@ static int32_t run_layers(Model* m, const int32_t* d_ids, int32_t B, int32_t poo
       FL_STAGE(FLETCHER_STAGE_ATTENTION,
                launch_flash_attention_tc(c, dt, qkv, qkv + H * es, qkv + 2 * H * es, 3 * H, T, H, m->CTX, H,
                                          m->d_cu, m->d_tiles, n_tiles, (int32_t)m->nh, scale));
-      FL_STAGE(FLETCHER_STAGE_GEMM_O, launch_gemm_residual_ln(c, dt, m->bn_o, m->CTX, T, H, L.wo, H, m->S, L.bo, m->X,
-                                                              L.ln1g, L.ln1b, eps, m->ln_cnt, nullptr));
+      FL_STAGE(FLETCHER_STAGE_GEMM_O, launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_o, m->CTX, T, H, L.wo, H, m->S, H, L.bo,
+                                                     m->X, H, nullptr, nullptr, nullptr, 0));
+      FL_STAGE(FLETCHER_STAGE_LAYERNORM, launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln1g, L.ln1b, T, H, eps));
       FL_STAGE(FLETCHER_STAGE_GEMM_UP, launch_gemm_tc(c, dt, swiglu ? EPI_SWIGLU : EPI_GELU, m->bn_up, m->X, T, H, L.wi,
                                                       Iup, m->ACT, I, L.bi, nullptr, 0, nullptr, nullptr, nullptr, 0));
-      FL_STAGE(FLETCHER_STAGE_GEMM_DOWN, launch_gemm_residual_ln(c, dt, m->bn_d, m->ACT, T, I, L.wd, H, m->S, L.bd,
-                                                                 m->X, L.ln2g, L.ln2b, eps, m->ln_cnt, nullptr));
+      FL_STAGE(FLETCHER_STAGE_GEMM_DOWN, launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_d, m->ACT, T, I, L.wd, H, m->S, H,
+                                                        L.bd, m->X, H, nullptr, nullptr, nullptr, 0));
+      FL_STAGE(FLETCHER_STAGE_LAYERNORM, launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln2g, L.ln2b, T, H, eps));
     }
   }
   if (pooling == FLETCHER_POOL_MEAN_L2) {
