@@ -310,12 +310,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (w + vstride < args.num_work) nxt = decode(args, w + vstride);
       float m_ref = 0.f, l = 0.f;
       bool ok = true;
+      // A warp whose 32 query rows all lie past the sequence end (the tail of its last tile)
+      // skips the softmax: its P and O rows are never stored.  It still follows S_full (S_{j+1}
+      // comes only after PV_j has read P_j) and arrives on every barrier, keeping the phases.
+      const bool live = wk.q0 + q * 32 < wk.L;
       for (int j = 0; j < wk.nb; j++, gs++) {
         if (!mbar_wait(B.s_full, gs & 1, abort, args.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        if (!live) {
+          tc_fence_before();
+          mbar_arrive(B.p_full);
+          continue;
+        }
         float sv[BKV];
         tmem_ld64(t_s, sv);
         const int valid = wk.L - j * BKV;  // keys of this block inside the sequence (>= 1)
@@ -364,6 +373,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       if (!ok || !mbar_wait(B.o_full, t & 1, abort, args.err)) break;
       tc_fence_after();
+      if (!live) {
+        tc_fence_before();
+        mbar_arrive(B.o_free);
+        continue;
+      }
       float o[D];
       tmem_ld64(t_o, o);
       tc_fence_before();
