@@ -11,7 +11,8 @@ enum Epi : int {
   EPI_GELU = 2,     // out = GeluFast(acc + bias)
   EPI_SWIGLU = 3,   // out[:, j] = silu(gate + bg) * (up + bu), W packed gate/up-interleaved
   EPI_RESIDUAL = 4,  // out = acc + bias + residual
-  EPI_PARTIAL = 5    // internal (split-K): fp32 sums of one K range to a workspace, finished later
+  EPI_PARTIAL = 5,   // internal (split-K): fp32 sums of one K range to a workspace, finished later
+  EPI_RESIDUAL_TMA = 6  // internal: EPI_RESIDUAL with the residual loaded by TMA (chosen for K <= 1024)
 };
 
 struct GemmArgs {

@@ -43,10 +43,15 @@ constexpr int kStageOut = 32 * 128;                    // per-warp output box: 3
 // Epilogues drained by alternating warp groups (see the epilogue section of k_gemm_tc).
 template <int EPI>
 constexpr bool kEpiGroups = EPI == 0 || EPI == 1 || EPI == 2 || EPI == 5;  // STORE, ROPE, GELU, PARTIAL
-// Output boxes in flight per warp: two where a warp writes four boxes per tile (the groups),
-// one for the residual and SwiGLU epilogues, whose shared memory goes to an extra operand stage.
+// Output boxes per warp: two where a warp writes four boxes per tile (the groups) and for the
+// TMA-residual epilogue (one per 64-column unit: each box arrives holding the residual rows and
+// leaves holding the sums); one for the register-residual and SwiGLU epilogues, whose shared
+// memory goes to an extra operand stage.
 template <int EPI>
-constexpr int kOutBufs = kEpiGroups<EPI> ? 2 : 1;
+constexpr int kOutBufs = kEpiGroups<EPI> || EPI == 6 ? 2 : 1;
+// Both residual epilogues: out = acc + bias + residual.
+template <int EPI>
+constexpr bool kResidual = EPI == 4 || EPI == 6;
 
 // PAIR: the tile is computed by a cluster of two CTAs on two SMs with tcgen05 cta_group::2
 // (M = 256 per MMA): each CTA loads its 128 rows of A and half of the tile's BN rows of W, and
@@ -61,12 +66,13 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int OUT_BYTES = kEpiWarps * OUT_BUFS * kStageOut;
   // As many operand stages as fit next to the output staging (at most 8).
-  static constexpr int STAGES_FIT = (232448 - 1024 - 256 - OUT_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES_FIT = (232448 - 1024 - 384 - OUT_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT < 8 ? STAGES_FIT : 8;
   static constexpr int OUT_OFF = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = OUT_OFF + OUT_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = BAR_OFF + 256 /*barriers*/ + 1024 /*alignment slack*/;
+  static constexpr int SMEM = BAR_OFF + 384 /*barriers*/ + 1024 /*alignment slack*/;
+  static_assert((2 * STAGES + 6 + 2 * kEpiWarps) * 8 <= 384, "barrier area");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -86,6 +92,8 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int r, const float (&a)[
 }
 
 // v[i] += the 32 16-bit values in q[0..3].
+// stage_row with the box's current contents (this row's 64 residual values, as TMA loaded
+// them) added: row = a|b + residual, in place.
 template <typename T>
 __device__ __forceinline__ void add_packed(float (&v)[32], const uint4* q4) {
 #pragma unroll
@@ -107,10 +115,34 @@ __device__ __forceinline__ void add_packed(float (&v)[32], const uint4* q4) {
   }
 }
 
+template <typename T>
+__device__ __forceinline__ void stage_row_add(uint8_t* buf, int r, const float (&a)[32], const float (&b)[32]) {
+  uint8_t* row = buf + r * 128;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const float* v = j < 4 ? &a[j * 8] : &b[(j - 4) * 8];
+    uint4* p = reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4));
+    const uint4 q = *p;
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    float f[8];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      float2 t;
+      if constexpr (std::is_same<T, __nv_bfloat16>::value)
+        t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+      else
+        t = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+      f[2 * k] = v[2 * k] + t.x;
+      f[2 * k + 1] = v[2 * k + 1] + t.y;
+    }
+    *p = make_uint4(pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]), pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
+  }
+}
+
 template <typename T, int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+              const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, const GemmArgs args) {
   using C = Cfg<BN, PAIR, kOutBufs<EPI>>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -124,6 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = bars + 2 * C::STAGES + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint64_t* rbar = bars + 2 * C::STAGES + 6;  // residual box loaded: one per epilogue warp and box
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = args.num_n_tiles;
@@ -150,12 +183,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[i], (kEpiGroups<EPI> ? kEpiWarps / 2 : kEpiWarps) * (PAIR ? 2 : 1));
     }
     *abort = 0;
+    if constexpr (EPI == EPI_RESIDUAL_TMA)
+      for (int i = 0; i < 2 * kEpiWarps; i++) mbar_init(&rbar[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0 && lane == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmC) : "memory");
+    if constexpr (EPI == EPI_RESIDUAL_TMA) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmR) : "memory");
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -269,6 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int col0 = GROUPS ? 0 : ((warp - 2) >> 2) * (EPI == EPI_SWIGLU ? 64 : BN / 2);
     uint8_t* stg0 = smem + C::OUT_OFF + (warp - 2) * kOutBufs<EPI> * kStageOut;
     int ob = 0;  // output buffer of the next box
+    uint32_t rph = 0;  // residual: phase bit of each box's load barrier
     // 64-column output units per warp: SwiGLU halves the width (BN/2 outputs per tile).
     constexpr int UNITS = (EPI == EPI_SWIGLU ? BN / 128 : BN / 64) / (GROUPS ? 1 : 2);
     const int tstep = GROUPS ? 2 : 1;
@@ -311,8 +348,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // Residual: each unit's 128 bytes of the row are requested before its accumulator load
-      // (the first unit's before the wait for the accumulator).
+      // Register residual: each unit's 128 bytes of the row are requested before its
+      // accumulator load (the first unit's before the wait for the accumulator).
       uint4 res[EPI == EPI_RESIDUAL ? 8 : 1];
       auto load_res = [&](int u) {
         if constexpr (EPI == EPI_RESIDUAL) {
@@ -326,6 +363,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       load_res(0);
+      // TMA residual: unit u's 32 x 64 box of the residual rows is loaded into the warp's output
+      // box u (free once the previous tile's stores have read it) before the wait for the
+      // accumulator; the sums are added into the box in place and stored from it.  Coalesced,
+      // and no row-per-lane loads through L1.
+      if constexpr (EPI == EPI_RESIDUAL_TMA) {
+        if (lane == 0) {
+          bulk_wait_read0();
+          if (row0 < args.M) {
+#pragma unroll
+            for (int u = 0; u < UNITS; u++) {
+              const int64_t oc = (int64_t)nb * BN + col0 + u * 64;
+              if (oc < args.N) {
+                uint64_t* rb = &rbar[(warp - 2) * 2 + u];
+                mbar_expect_tx(rb, kStageOut);
+                tma_load_2d(stg0 + u * kStageOut, &tmR, rb, (int)oc, row0);
+              }
+            }
+          }
+        }
+        __syncwarp();
+      }
       if (!mbar_wait_spin(&tfull[acc], acc_phase, abort, args.err)) break;
       tc_fence_after();
 #pragma unroll 1
@@ -421,19 +479,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else if (ocol < n_out && row0 < args.M) {
           uint8_t* stg = stg0 + ob * kStageOut;
-          if (lane == 0) {  // the box stored from this buffer has left it
-            if constexpr (kOutBufs<EPI> == 2)
-              bulk_wait_read1();
-            else
-              bulk_wait_read0();
+          if constexpr (EPI == EPI_RESIDUAL_TMA) {  // box u holds this unit's residual rows
+            stg = stg0 + u * kStageOut;
+            if (!mbar_wait_spin(&rbar[(warp - 2) * 2 + u], (rph >> u) & 1, abort, args.err)) break;
+            rph ^= 1u << u;
+            stage_row_add<T>(stg, lane, a, b);
+          } else {
+            if (lane == 0) {  // the box stored from this buffer has left it
+              if constexpr (kOutBufs<EPI> == 2)
+                bulk_wait_read1();
+              else
+                bulk_wait_read0();
+            }
+            __syncwarp();
+            stage_row<T>(stg, lane, a, b);
           }
-          __syncwarp();
-          stage_row<T>(stg, lane, a, b);
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
             // rows >= M are clipped by TMA; the residual sum is kept in L2 for the LayerNorm after it
-            if constexpr (EPI == EPI_RESIDUAL)
+            if constexpr (kResidual<EPI>)
               tma_store_2d_keep(&tmC, stg, (int)ocol, row0);
             else
               tma_store_2d(&tmC, stg, (int)ocol, row0);
@@ -579,7 +644,8 @@ static int32_t make_map(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, 
 }
 
 template <typename T, int BN, int EPI, bool PAIR>
-static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmArgs a) {
+static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr,
+                   GemmArgs a) {
   using Cf = Cfg<BN, PAIR, kOutBufs<EPI>>;
   auto kern = k_gemm_tc<T, BN, EPI, PAIR>;
   static bool attr_set[64] = {};  // per device
@@ -606,10 +672,10 @@ static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const C
     at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 2;
-    FL_CUDA(c, cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, a));
+    FL_CUDA(c, cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mr, a));
   } else {
     const int grid = tiles < c->num_sms ? tiles : c->num_sms;
-    FL_CUDA(c, launch_pdl(kern, dim3(grid), dim3(kThreads), Cf::SMEM, c->stream, ma, mb, mc, a));
+    FL_CUDA(c, launch_pdl(kern, dim3(grid), dim3(kThreads), Cf::SMEM, c->stream, ma, mb, mc, mr, a));
   }
   FL_LAUNCH(c);
   return FLETCHER_OK;
@@ -617,19 +683,20 @@ static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const C
 
 template <typename T, bool PAIR>
 static int32_t dispatch(Ctx* c, int epi, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
-                        const GemmArgs& a) {
+                        const CUtensorMap& mr, const GemmArgs& a) {
 #define FL_EPI(E)                                                                            \
   case E:                                                                                    \
-    return bn == 256 ? run<T, 256, E, PAIR>(c, ma, mb, mc, a) : run<T, 128, E, PAIR>(c, ma, mb, mc, a);
+    return bn == 256 ? run<T, 256, E, PAIR>(c, ma, mb, mc, mr, a) : run<T, 128, E, PAIR>(c, ma, mb, mc, mr, a);
   switch (epi) {
     FL_EPI(EPI_STORE)
     FL_EPI(EPI_ROPE)
     FL_EPI(EPI_GELU)
     FL_EPI(EPI_RESIDUAL)
+    FL_EPI(EPI_RESIDUAL_TMA)
     case EPI_SWIGLU:
-      return run<T, 256, EPI_SWIGLU, PAIR>(c, ma, mb, mc, a);
+      return run<T, 256, EPI_SWIGLU, PAIR>(c, ma, mb, mc, mr, a);
     case EPI_PARTIAL:
-      return run<T, 128, EPI_PARTIAL, false>(c, ma, mb, mc, a);
+      return run<T, 128, EPI_PARTIAL, false>(c, ma, mb, mc, mr, a);
   }
 #undef FL_EPI
   return set_error(c, FLETCHER_ERR_INVALID, "gemm: unknown epilogue %d", epi);
@@ -686,9 +753,9 @@ static int32_t launch_gemm_splitk(Ctx* c, int32_t dtype, int epi, const void* A,
   a.kb_per = kb_per;
   a.partial = c->splitk;
   if (dtype == FLETCHER_BF16)
-    rc = tc::dispatch<__nv_bfloat16, false>(c, EPI_PARTIAL, 128, ma, mb, ma, a);
+    rc = tc::dispatch<__nv_bfloat16, false>(c, EPI_PARTIAL, 128, ma, mb, ma, ma, a);
   else
-    rc = tc::dispatch<__half, false>(c, EPI_PARTIAL, 128, ma, mb, ma, a);
+    rc = tc::dispatch<__half, false>(c, EPI_PARTIAL, 128, ma, mb, ma, ma, a);
   if (rc) return rc;
   const int64_t n_out = epi == EPI_SWIGLU ? N / 2 : N;
   const int64_t pairs = M * (n_out / 2);
@@ -759,6 +826,13 @@ int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, in
   if (rc) return rc;
   rc = tc::make_map(c, &mc, dtype, out, (uint64_t)M, (uint64_t)n_out, (uint64_t)ld_out, 64, 32);
   if (rc) return rc;
+  // Short-K residual GEMMs are epilogue-bound: their residual rows come by TMA into the output
+  // boxes.  Long-K ones keep the register path and the extra operand stage it leaves.
+  if (epi == EPI_RESIDUAL && K <= 1024) epi = EPI_RESIDUAL_TMA;
+  CUtensorMap mr = mc;  // the residual rows, read as the output boxes they are added into
+  if (epi == EPI_RESIDUAL_TMA &&
+      (rc = tc::make_map(c, &mr, dtype, residual, (uint64_t)M, (uint64_t)N, (uint64_t)ld_res, 64, 32)))
+    return rc;
   GemmArgs a{};
   a.M = M;
   a.N = N;
@@ -776,11 +850,11 @@ int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, in
   a.splits = 1;
   a.kb_per = (int)(K / tc::BK);
   if (pair) {
-    if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16, true>(c, epi, bn, ma, mb, mc, a);
-    return tc::dispatch<__half, true>(c, epi, bn, ma, mb, mc, a);
+    if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16, true>(c, epi, bn, ma, mb, mc, mr, a);
+    return tc::dispatch<__half, true>(c, epi, bn, ma, mb, mc, mr, a);
   }
-  if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16, false>(c, epi, bn, ma, mb, mc, a);
-  return tc::dispatch<__half, false>(c, epi, bn, ma, mb, mc, a);
+  if (dtype == FLETCHER_BF16) return tc::dispatch<__nv_bfloat16, false>(c, epi, bn, ma, mb, mc, mr, a);
+  return tc::dispatch<__half, false>(c, epi, bn, ma, mb, mc, mr, a);
 }
 
 }  // namespace fl

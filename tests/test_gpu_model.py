@@ -66,7 +66,8 @@ def test_cfg1_full_batch_f32(be, oracle_mod):
 
 
 @pytest.mark.parametrize("lengths", [[1], [2, 1, 3], [63, 64, 65], [127, 128, 129, 1], [300, 17],
-                                     [2048, 700, 64]])  # cfg4 long context
+                                     [700, 601],  # single-SM tiles, no split-K (1024 < T < 2048)
+                                     [2048, 700, 64]])  # cfg4 long context; 2-SM tiles
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_edge_lengths_nomic(be, oracle_mod, lengths, dtype):
     cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
