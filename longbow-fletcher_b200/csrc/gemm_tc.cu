@@ -305,7 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int col0 = GROUPS ? 0 : ((warp - 2) >> 2) * (EPI == EPI_SWIGLU ? 64 : BN / 2);
     uint8_t* stg0 = smem + C::OUT_OFF + (warp - 2) * kOutBufs<EPI> * kStageOut;
     int ob = 0;  // output buffer of the next box
-    uint32_t rph = 0;  // residual: phase bit of each box's load barrier
+    uint32_t rph = 0;    // residual: phase bit of each box's load barrier
+    uint32_t rpend = 0;  // residual: boxes whose load is issued and not yet waited for
     // 64-column output units per warp: SwiGLU halves the width (BN/2 outputs per tile).
     constexpr int UNITS = (EPI == EPI_SWIGLU ? BN / 128 : BN / 64) / (GROUPS ? 1 : 2);
     const int tstep = GROUPS ? 2 : 1;
@@ -368,13 +369,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // accumulator; the sums are added into the box in place and stored from it.  Coalesced,
       // and no row-per-lane loads through L1.
       if constexpr (EPI == EPI_RESIDUAL_TMA) {
-        if (lane == 0) {
-          bulk_wait_read0();
-          if (row0 < args.M) {
+        if (lane == 0) bulk_wait_read0();
+        if (row0 < args.M) {
 #pragma unroll
-            for (int u = 0; u < UNITS; u++) {
-              const int64_t oc = (int64_t)nb * BN + col0 + u * 64;
-              if (oc < args.N) {
+          for (int u = 0; u < UNITS; u++) {
+            const int64_t oc = (int64_t)nb * BN + col0 + u * 64;
+            if (oc < args.N) {
+              rpend |= 1u << u;
+              if (lane == 0) {
                 uint64_t* rb = &rbar[(warp - 2) * 2 + u];
                 mbar_expect_tx(rb, kStageOut);
                 tma_load_2d(stg0 + u * kStageOut, &tmR, rb, (int)oc, row0);
@@ -483,6 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             stg = stg0 + u * kStageOut;
             if (!mbar_wait_spin(&rbar[(warp - 2) * 2 + u], (rph >> u) & 1, abort, args.err)) break;
             rph ^= 1u << u;
+            rpend &= ~(1u << u);
             stage_row_add<T>(stg, lane, a, b);
           } else {
             if (lane == 0) {  // the box stored from this buffer has left it
@@ -509,6 +512,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (lane == 0) bulk_wait0();
+    if constexpr (EPI == EPI_RESIDUAL_TMA) {
+      // Left early (aborting): this warp's residual loads land before the CTA exits.
+      for (int u = 0; u < 2; u++)
+        if ((rpend >> u) & 1)
+          for (int i = 0; i < (1 << 22) && !mbar_try(&rbar[(warp - 2) * 2 + u], (rph >> u) & 1); i++) {
+          }
+    }
   }
 
   tc_fence_before();
