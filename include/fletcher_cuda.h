@@ -98,6 +98,11 @@ int32_t Cuda_Synchronize(CudaContextRef ctx);
 void* Cuda_GetStream(CudaContextRef ctx);
 /* Number of kernels this context has launched so far (for launch accounting). */
 int64_t Cuda_GetLaunchCount(CudaContextRef ctx);
+/* Test hook without a counterpart in the reference: runs the bounded device wait that every
+ * tensor-core kernel uses on an mbarrier that nothing completes, with a limit of limit_cycles
+ * (0 < limit <= the production limit of about 2 s); sleeping selects the sleeping wait, else the
+ * spinning one.  Expected result: FLETCHER_ERR_DEVICE_WAIT, with the context still usable. */
+int32_t Cuda_Debug_WaitTimeoutProbe(CudaContextRef ctx, int64_t limit_cycles, int32_t sleeping);
 /* device.Backend.GetVRAMUsage (device.go:161): bytes held by this context's buffers, and
  * the device's total memory. */
 int32_t Cuda_MemGetInfo(CudaContextRef ctx, int64_t* allocated, int64_t* total);

@@ -45,13 +45,14 @@ __device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity) {
 }
 // Bounded spin wait (latency first; for kernels whose waiting threads do not compete with
 // compute warps for issue slots).  Returns false when this CTA is aborting.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort, int32_t* err) {
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort, int32_t* err,
+                                               long long limit = kWaitLimitCycles) {
   const long long t0 = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try(bar, parity)) return true;
     if ((i & 255) == 0) {
       if (*abort) return false;
-      if (clock64() - t0 > kWaitLimitCycles) {
+      if (clock64() - t0 > limit) {
         atomicExch(err, kDevWaitTimeout);
         *abort = 1;
         return false;
@@ -60,13 +61,14 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, v
   }
 }
 // Bounded sleeping wait.  Returns false when this CTA is aborting (timeout here or elsewhere).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int32_t* err) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int32_t* err,
+                                          long long limit = kWaitLimitCycles) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_sleep(bar, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       atomicExch(err, kDevWaitTimeout);
       *abort = 1;
       return false;

@@ -92,6 +92,7 @@ def _sig(L):
         "Cuda_Model_SetGraphs": (i32, [vp, i32]),
         "Cuda_Model_StageTimes": (i32, [vp, f32p, i64p, i32]),
         "Cuda_GetLaunchCount": (i64, [vp]),
+        "Cuda_Debug_WaitTimeoutProbe": (i32, [vp, i64, i32]),
         "Cuda_Model_Free": (i32, [vp]),
     }
     for name, (res, args) in sigs.items():
