@@ -37,7 +37,7 @@ constexpr int KV_BYTES = BKV * D * 2;
 // Per slot: Q, K[2], V[2] (each 1024-byte aligned).
 constexpr int SLOT_Q = 0, SLOT_K = Q_BYTES, SLOT_V = Q_BYTES + 2 * KV_BYTES;
 constexpr int SLOT_BYTES = Q_BYTES + 4 * KV_BYTES;
-constexpr int kBarsPerSlot = 10;
+constexpr int kBarsPerSlot = 11;
 constexpr int OFF_BAR = kSlots * SLOT_BYTES;
 constexpr int SMEM = OFF_BAR + kSlots * kBarsPerSlot * 8 + 16 + 1024;
 constexpr int TMEM_COLS = 256;  // slot s: S [128s, 128s+64) with P in its upper 32 columns, O [128s+64, 128s+128)
@@ -60,10 +60,10 @@ struct Work {
 
 // Barriers of one slot.
 struct SlotBars {
-  uint64_t *q_full, *q_empty, *kv_full, *kv_empty, *s_full, *p_full, *o_full, *o_free;
+  uint64_t *q_full, *q_empty, *kv_full, *kv_empty, *s_full, *p_full, *o_full, *o_free, *drain;
   __device__ SlotBars(uint64_t* b)
       : q_full(b), q_empty(b + 1), kv_full(b + 2), kv_empty(b + 4), s_full(b + 6), p_full(b + 7), o_full(b + 8),
-        o_free(b + 9) {}
+        o_free(b + 9), drain(b + 10) {}
 };
 
 // 2^x on the SFU (one instruction; -inf -> 0).
@@ -192,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(B.p_full, 128);
       mbar_init(B.o_full, 1);
       mbar_init(B.o_free, 128);
+      mbar_init(B.drain, 1);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -223,10 +224,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t id_s = idesc<T, BQ, BKV>();
       const uint32_t id_o = idesc<T, BQ, D, true>();
       uint32_t gl = 0, gc = 0, gs = 0;  // K/V blocks loaded, K/V blocks consumed, S blocks
+      uint32_t qn = 0, qw = 0;          // Q tiles loaded, Q tiles waited for
       auto load_q = [&](const Work& wk, uint32_t t) -> bool {
         if (!mbar_wait(B.q_empty, (t & 1) ^ 1, abort, args.err)) return false;
         mbar_expect_tx(B.q_full, Q_BYTES);
         tma_load_2d(sb + SLOT_Q, &tmQ, B.q_full, wk.h * D, wk.start + wk.q0);
+        qn++;
         return true;
       };
       auto load_kv = [&](const Work& wk, int j) -> bool {
@@ -259,7 +262,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           const bool has_next = wn < args.num_work;
           Work nxt{};
           if (has_next) nxt = decode(args, wn);
-          if (!mbar_wait(B.q_full, t & 1, abort, args.err) || !issue_s()) break;
+          if (!mbar_wait(B.q_full, t & 1, abort, args.err)) break;
+          qw++;
+          if (!issue_s()) break;
           if (cur.nb == 1) mma_commit(B.q_empty);  // Q free once the item's last S ran
           if (nl < cur.nb && !(ok = load_kv(cur, nl++))) break;
           for (int j = 0; j < cur.nb && ok; j++) {
@@ -291,6 +296,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           cur = nxt;
           nl = 1;
         }
+      }
+      if (*abort) {  // leaving early: this slot's MMAs and loads land before TMEM is freed
+        mma_commit(B.drain);
+        mbar_drain(B.drain, 0);
+        for (uint32_t i = gc; i < gl; i++) mbar_drain(&B.kv_full[i & 1], (i >> 1) & 1);
+        if (qn > qw) mbar_drain(B.q_full, (qn - 1) & 1);
       }
     }
   } else {

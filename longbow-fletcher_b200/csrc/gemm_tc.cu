@@ -72,7 +72,7 @@ struct Cfg {
   static constexpr int BAR_OFF = OUT_OFF + OUT_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM = BAR_OFF + 384 /*barriers*/ + 1024 /*alignment slack*/;
-  static_assert((2 * STAGES + 6 + 2 * kEpiWarps) * 8 <= 384, "barrier area");
+  static_assert((2 * STAGES + 7 + 2 * kEpiWarps) * 8 <= 384, "barrier area");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint64_t* rbar = bars + 2 * C::STAGES + 6;  // residual box loaded: one per epilogue warp and box
+  uint64_t* drain = rbar + 2 * kEpiWarps;      // an aborting MMA thread's issued MMAs are complete
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = args.num_n_tiles;
@@ -183,6 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[i], (kEpiGroups<EPI> ? kEpiWarps / 2 : kEpiWarps) * (PAIR ? 2 : 1));
     }
     *abort = 0;
+    mbar_init(drain, 1);
     if constexpr (EPI == EPI_RESIDUAL_TMA)
       for (int i = 0; i < 2 * kEpiWarps; i++) mbar_init(&rbar[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -219,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      uint32_t issued = 0, issued_par = 0;  // per stage: loaded at least once; parity of the last load
       for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
         const int mb = tile / splits / n_tiles, nb = tile / splits % n_tiles;
         int kb0, kb1;
@@ -238,13 +241,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BK, a_row);
             tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BK, b_row);
           }
+          issued |= 1u << stage;
+          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-    producer_done:;
+    producer_done:
+      // Aborting: the operand loads still in flight land before the CTA exits.  In pair mode
+      // both CTAs' loads complete on the even CTA's barriers, which that CTA drains.
+      if (*abort && crank == 0)
+        for (int s = 0; s < C::STAGES; s++)
+          if ((issued >> s) & 1) mbar_drain(&full[s], (issued_par >> s) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0 && crank == 0) {
@@ -290,6 +300,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit_pair(&tfull[acc]);
         else
           mma_commit(&tfull[acc]);
+      }
+      if (*abort) {  // the MMAs issued so far complete before TMEM is freed
+        if constexpr (PAIR)
+          mma_commit_pair(drain);
+        else
+          mma_commit(drain);
+        mbar_drain(drain, 0);
       }
     }
   } else {
@@ -515,9 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (EPI == EPI_RESIDUAL_TMA) {
       // Left early (aborting): this warp's residual loads land before the CTA exits.
       for (int u = 0; u < 2; u++)
-        if ((rpend >> u) & 1)
-          for (int i = 0; i < (1 << 22) && !mbar_try(&rbar[(warp - 2) * 2 + u], (rph >> u) & 1); i++) {
-          }
+        if ((rpend >> u) & 1) mbar_drain(&rbar[(warp - 2) * 2 + u], (rph >> u) & 1);
     }
   }
 

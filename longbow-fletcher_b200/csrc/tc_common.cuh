@@ -76,6 +76,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait for a phase on the way out of an aborting kernel (it ignores the abort flag):
+// lets the copies and MMAs this thread issued land before the CTA frees its TMEM and exits.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  for (int i = 0; i < (1 << 22) && !mbar_try(bar, parity); i++) {
+  }
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
