@@ -22,6 +22,7 @@
 //               O (complete, because S_j's commit follows PV_{j-1}) is rescaled in TMEM.  At the end of an item the row of O is divided by its sum and stored.
 // TMEM per slot: S/P 64 columns + O 64 columns; 256 per CTA.  ~98 KB smem.  All mbarrier waits
 // are bounded (device error flag + abort, as in the GEMM).  No multicast.
+#include <atomic>
 #include "tc_common.cuh"
 
 namespace fl {
@@ -449,14 +450,15 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void*
   const int work = num_tiles * nh;
   const int st256 = ((uintptr_t)out & 31) == 0 && (ld_out * 2) % 32 == 0;
   AttnArgs a{cu, tiles128, work, nh, out, ld_out, scale * 1.4426950408889634f, c->d_err, st256};
-  static bool attr_set[2][64] = {};
+  // Per dtype and device; host threads of several replicas may get here at once (idempotent).
+  static std::atomic<bool> attr_set[2][64] = {};
   const int ti = dt == FLETCHER_BF16 ? 0 : 1;
-  if (!attr_set[ti][c->device & 63]) {
+  if (!attr_set[ti][c->device & 63].load(std::memory_order_acquire)) {
     if (dt == FLETCHER_BF16)
       FL_CUDA(c, cudaFuncSetAttribute(k_attn_tc<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     else
       FL_CUDA(c, cudaFuncSetAttribute(k_attn_tc<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-    attr_set[ti][c->device & 63] = true;
+    attr_set[ti][c->device & 63].store(true, std::memory_order_release);
   }
   const int want = (work + kSlots - 1) / kSlots;
   const int grid = want < 2 * c->num_sms ? want : 2 * c->num_sms;

@@ -27,6 +27,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
+#include <atomic>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -680,10 +681,11 @@ static int32_t run(Ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const C
                    GemmArgs a) {
   using Cf = Cfg<BN, PAIR, kOutBufs<EPI>>;
   auto kern = k_gemm_tc<T, BN, EPI, PAIR>;
-  static bool attr_set[64] = {};  // per device
-  if (!attr_set[c->device & 63]) {
+  // Per device; host threads of several replicas may get here at once (the call is idempotent).
+  static std::atomic<bool> attr_set[64] = {};
+  if (!attr_set[c->device & 63].load(std::memory_order_acquire)) {
     FL_CUDA(c, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
-    attr_set[c->device & 63] = true;
+    attr_set[c->device & 63].store(true, std::memory_order_release);
   }
   a.num_m_tiles = (int)((a.M + Cf::TILE_M - 1) / Cf::TILE_M);
   a.num_n_tiles = (int)((a.N + BN - 1) / BN);
