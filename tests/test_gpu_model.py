@@ -209,3 +209,16 @@ def test_async_batches_match_sync(be):
         assert np.array_equal(bo.array, w)
         bi.close()
         bo.close()
+
+
+
+@pytest.mark.parametrize("lengths", [[700, 601], [2048, 700, 64]])
+def test_fp16_tiled_paths_nomic(be, oracle_mod, lengths):
+    """fp16 through the non-split GEMMs (single-SM and 2-SM tiles, both residual epilogues)."""
+    cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
+    lens = np.array(lengths, np.int32)
+    ids = synth.make_ids(lens, cfg.vocab_size, 23)
+    blob = synth.make_weights(cfg, 1)
+    want = oracle_mod.forward(cfg, blob, ids, lens)
+    got = model(be, cfg, "f16", 1).forward_batch(ids, lens, 1)
+    assert_close_16(got, want["mean"], f"f16 {lengths}")
