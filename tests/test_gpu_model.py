@@ -222,3 +222,25 @@ def test_fp16_tiled_paths_nomic(be, oracle_mod, lengths):
     want = oracle_mod.forward(cfg, blob, ids, lens)
     got = model(be, cfg, "f16", 1).forward_batch(ids, lens, 1)
     assert_close_16(got, want["mean"], f"f16 {lengths}")
+
+
+# BERT-base shape (GELU, absolute positions, biases) from bert-tiny's architecture.
+BERT_BASE_2L = dataclasses.replace(synth.BERT_TINY, hidden=768, num_heads=12, intermediate=3072, num_layers=2)
+
+
+@pytest.mark.parametrize("cfg_name,lengths", [
+    ("base", [512, 512, 500, 400, 300, 512, 200]),  # 2,936 tokens: 2-SM tiles
+    ("base", [512, 500, 301]),                      # 1,313 tokens: single-SM tiles, no split-K
+    ("tiny", [128] * 20 + [77] * 30 + [5] * 9),      # 4,915 tokens: tiled, 128-wide tiles
+])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_gelu_absolute_tiled_paths(be, oracle_mod, cfg_name, lengths, dtype):
+    """The GELU epilogue, absolute positions and both poolers through the non-split GEMMs."""
+    cfg = BERT_BASE_2L if cfg_name == "base" else synth.BERT_TINY
+    lens = np.array(lengths, np.int32)
+    ids = synth.make_ids(lens, cfg.vocab_size, 31)
+    blob = synth.make_weights(cfg, 3)
+    want = oracle_mod.forward(cfg, blob, ids, lens)
+    m = model(be, cfg, dtype, 3)
+    assert_close_16(m.forward_batch(ids, lens, 1), want["mean"], f"{cfg_name} {dtype} mean")
+    assert_close_16(m.forward_batch(ids, lens, 0), want["cls"], f"{cfg_name} {dtype} cls")
