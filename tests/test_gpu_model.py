@@ -244,3 +244,16 @@ def test_gelu_absolute_tiled_paths(be, oracle_mod, cfg_name, lengths, dtype):
     m = model(be, cfg, dtype, 3)
     assert_close_16(m.forward_batch(ids, lens, 1), want["mean"], f"{cfg_name} {dtype} mean")
     assert_close_16(m.forward_batch(ids, lens, 0), want["cls"], f"{cfg_name} {dtype} cls")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_absolute_positions_clamp_past_max(be, oracle_mod, dtype):
+    """Rows at or past max_positions (512 for bert-tiny) use the last position row (bert.go's
+    clamp to max - 1)."""
+    cfg = synth.BERT_TINY
+    lens = np.array([600, 30, 513], np.int32)
+    ids = synth.make_ids(lens, cfg.vocab_size, 41)
+    blob = synth.make_weights(cfg, 3)
+    want = oracle_mod.forward(cfg, blob, ids, lens)
+    got = model(be, cfg, dtype, 3).forward_batch(ids, lens, 1)
+    (assert_close_f32 if dtype == "f32" else assert_close_16)(got, want["mean"], f"{dtype} clamp")
