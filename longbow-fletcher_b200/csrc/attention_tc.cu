@@ -117,30 +117,26 @@ __device__ __forceinline__ float row_max(const float (&sv)[BKV]) {
   return max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
 }
 
-// Largest P between reference-max updates: 2^64 for bf16 (fp32 O and row sums stay far from
+// Largest P (checked through the row sum, which bounds it) between reference-max updates: 2^64 for bf16 (fp32 O and row sums stay far from
 // overflow), 2^15 for fp16 (its largest finite value is 65504).
 template <typename T>
 __device__ __forceinline__ float kPMax() {
   return std::is_same<T, __nv_bfloat16>::value ? 18446744073709551616.0f : 32768.0f;
 }
 
-// P = 2^(S * scale * log2 e - ms) for a 64-key row: 16-bit pairs in pk, fp32 sum in `sum`;
-// returns the largest P.
+// P = 2^(S * scale * log2 e - ms) for a 64-key row: 16-bit pairs in pk, fp32 sum in `sum`.
 template <typename T>
-__device__ __forceinline__ float exp_row(float (&sv)[BKV], float sl2, float ms, uint32_t (&pk)[32], float& sum) {
+__device__ __forceinline__ void exp_row(float (&sv)[BKV], float sl2, float ms, uint32_t (&pk)[32], float& sum) {
   float ra[4][2] = {};  // four independent packed partial sums
-  float pm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int i = 0; i < BKV; i += 2) {
     fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
     sv[i] = ex2(sv[i]);
     sv[i + 1] = ex2(sv[i + 1]);
     add2(ra[(i >> 1) & 3][0], ra[(i >> 1) & 3][1], sv[i], sv[i + 1]);
-    pm[(i >> 1) & 3] = max3(pm[(i >> 1) & 3], sv[i], sv[i + 1]);
     pk[i >> 1] = pack2<T>(sv[i], sv[i + 1]);
   }
   sum = ((ra[0][0] + ra[0][1]) + (ra[1][0] + ra[1][1])) + ((ra[2][0] + ra[2][1]) + (ra[3][0] + ra[3][1]));
-  return fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
 }
 
 __device__ __forceinline__ Work decode(const AttnArgs& a, int w) {
@@ -347,8 +343,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (j == 0) m_ref = sv[0];
         float rsum;
         uint32_t pk[32];
-        const float pmax = exp_row<T>(sv, sl2, m_ref * sl2, pk, rsum);
-        const bool need = !(pmax <= kPMax<T>());
+        exp_row<T>(sv, sl2, m_ref * sl2, pk, rsum);
+        // The row sum bounds every P of the row, so a sum within the P range proves that no P
+        // left it (a NaN fails the test too).  A sum beyond the range with every P inside it only
+        // costs a needless rescale.
+        const bool need = !(rsum <= kPMax<T>());
         if (__any_sync(0xffffffffu, need)) {
           // Rare path: some row's max moved by more than the P range allows.  S is still in
           // TMEM (P is not written yet); O holds PV_0..PV_{j-1} complete (S_j's commit came
