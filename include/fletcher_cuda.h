@@ -48,6 +48,14 @@ enum {
 /* ---- device.DataType (device.go:119-124) + BFloat16 */
 enum { FLETCHER_F32 = 0, FLETCHER_F16 = 1, FLETCHER_BF16 = 2 };
 
+/* ---- fp32 <-> fp16 conversion of host-facing copies (Cuda_SetHalfConversion).
+ * REFERENCE (the default) reproduces the reference's Float32ToFloat16 / Float16ToFloat32
+ * (internal/device/utils.go:13-91), which its fp16 CUDA backend applies to CopyFromFloat32,
+ * Set and ToHost (cuda_linux.go:128,148,163): mantissa truncated, |x| < 2^-14 flushed to a
+ * signed zero, finite values saturated to +-65504 (0x7BFF), NaN -> 0x7E00, and fp16
+ * subnormals read back as +0.  RNE is IEEE round-to-nearest-even with gradual underflow. */
+enum { FLETCHER_HALF_REFERENCE = 0, FLETCHER_HALF_RNE = 1 };
+
 /* ---- device.ActivationType (device.go:126-134) */
 enum {
   FLETCHER_ACT_IDENTITY = 0,
@@ -106,6 +114,12 @@ int32_t Cuda_Debug_WaitTimeoutProbe(CudaContextRef ctx, int64_t limit_cycles, in
 /* device.Backend.GetVRAMUsage (device.go:161): bytes held by this context's buffers, and
  * the device's total memory. */
 int32_t Cuda_MemGetInfo(CudaContextRef ctx, int64_t* allocated, int64_t* total);
+/* Selects the fp16 conversion (FLETCHER_HALF_REFERENCE or FLETCHER_HALF_RNE) used from now on
+ * by this context's Cuda_CopyFromFloat32, Cuda_ToHostFloat32, Cuda_At, Cuda_Set, Cuda_Cast,
+ * the fp16 output of Cuda_Model_ForwardBatchEx/Async and the fp16 packing of Cuda_Model_LoadRaw.
+ * The reference's backend has only its own conversion (utils.go:13-91); RNE has no
+ * counterpart there. */
+int32_t Cuda_SetHalfConversion(CudaContextRef ctx, int32_t mode);
 
 /* ================================================================ buffers
  * Cuda_Alloc: cuda_bridge.h:25 (size in bytes, dtype f32).  Cuda_AllocTensor allocates
@@ -125,6 +139,21 @@ int32_t Cuda_BufferInfo(CudaBufferRef buf, int64_t* rows, int64_t* cols, int32_t
  * or from the buffer's dtype on the device (cuda_linux.go:139-169 converts on the host). */
 int32_t Cuda_CopyFromFloat32(CudaBufferRef buf, const float* data, int64_t count);
 int32_t Cuda_ToHostFloat32(CudaBufferRef buf, float* data, int64_t count);
+/* device.Tensor.At / Set (device.go:14-15; cuda_linux.go:119-133): one element (row, col) of a
+ * (rows, cols) buffer, read into or written from a float32, fp16 with the context's
+ * conversion.  Synchronous. */
+int32_t Cuda_At(CudaBufferRef buf, int64_t row, int64_t col, float* value);
+int32_t Cuda_Set(CudaBufferRef buf, int64_t row, int64_t col, float value);
+/* device.Tensor.Copy (cpu_backend.go:259-286, cuda_linux.go:171-174): count elements from
+ * src[srcOffset..] to dst[dstOffset..] on the device, converted to dst's dtype when the
+ * dtypes differ.  Offsets and count are in elements. */
+int32_t Cuda_Copy(CudaContextRef ctx, CudaBufferRef dst, int64_t dstOffset, CudaBufferRef src,
+                  int64_t srcOffset, int64_t count);
+/* device.Tensor.Slice(i, k, j, l) (cpu_backend.go:288-303): dst (a dense (k-i, l-j) buffer of
+ * src's dtype) receives a COPY of src[i:k, j:l], as the reference's CPU backend returns a copy,
+ * not a view.  k > i and l > j, as the reference panics otherwise. */
+int32_t Cuda_Slice(CudaContextRef ctx, CudaBufferRef src, int64_t i, int64_t k, int64_t j, int64_t l,
+                   CudaBufferRef dst);
 
 /* ================================================================ tensor ops
  * All tensors are row-major and dense.  Buffers of one op share a dtype except where noted
@@ -132,10 +161,20 @@ int32_t Cuda_ToHostFloat32(CudaBufferRef buf, float* data, int64_t count);
 
 /* cuda_bridge.h:33-36 (device.Tensor.Linear / LinearActivation, cpu_backend.go:612-660):
  * result = act(input[rows,inCols] . weight[inCols,outCols] + bias).  For SwiGLU the
- * result has outCols/2 columns.  bias may be NULL. */
+ * result has outCols/2 columns.  bias may be NULL.  For 16-bit buffers the tensor-core layout
+ * of the weight (K-major, SwiGLU-interleaved) and the fp32 bias are built on the first call
+ * and kept with the weight / bias buffer until that buffer is written through this ABI
+ * (any call that outputs to it, Cuda_CopyToDevice, Cuda_CopyFromFloat32, Cuda_Set) or its
+ * device pointer is handed out by Cuda_GetBufferContents, which invalidate them. */
 int32_t Cuda_Linear_Fused(CudaContextRef ctx, CudaBufferRef input, int64_t rows, int64_t inCols,
                           CudaBufferRef weight, int64_t outCols, CudaBufferRef bias,
                           CudaBufferRef result, int32_t activation);
+/* device.Tensor.Mul(a, b) with the T() view flag of each operand (cpu_backend.go:306-372):
+ * c[m, n] = op(a) . op(b), alpha 1 / beta 0, fp32 accumulation.  a is stored dense as [m, k]
+ * (transA = 0) or [k, m] (transA = 1); b as [k, n] (transB = 0) or [n, k] (transB = 1); all
+ * three share one dtype.  16-bit products with transA = 0 run on the tensor cores. */
+int32_t Cuda_Mul(CudaContextRef ctx, CudaBufferRef a, int32_t transA, CudaBufferRef b, int32_t transB,
+                 CudaBufferRef c, int64_t m, int64_t n, int64_t k);
 /* cuda_bridge.h:38-40 (cpu_backend.go:541-601).  input may equal result. */
 int32_t Cuda_LayerNorm(CudaContextRef ctx, CudaBufferRef input, CudaBufferRef gamma,
                        CudaBufferRef beta, CudaBufferRef result, int64_t rows, int64_t cols,
@@ -210,13 +249,34 @@ int32_t Cuda_Model_Create(CudaContextRef ctx, const FletcherBertConfig* cfg, int
  * (internal/embeddings/weights/loader.go:29-90); count must equal Cuda_Model_WeightCount. */
 int32_t Cuda_Model_LoadRaw(CudaModelRef model, const float* blob, int64_t count);
 int64_t Cuda_Model_WeightCount(const FletcherBertConfig* cfg);
+/* One checkpoint tensor, by its name in the reference's SafeTensors loader (LoadFromSafeTensors,
+ * internal/embeddings/weights/loader.go:155-296: "embeddings.word_embeddings.weight",
+ * "encoder.layer.3.attention.self.query.weight", "pooler.dense.bias", ...), straight from host
+ * memory in its stored dtype (FLETCHER_F32, F16 or BF16) into the model's device layout: no
+ * host fp32 copy of the model is made (the reference widens on the host and rejects F16,
+ * loader.go:210-215).  rows x cols is the tensor as given; transposed = 1 marks a Linear weight
+ * stored (out, in), the PyTorch layout that loader.go:229-251 transposes; 0 means (in, out).
+ * Only Linear weights (2-D ".weight" outside the embeddings and LayerNorms) may be transposed.
+ * Errors follow the loader: unknown name, size or shape mismatch -> FLETCHER_ERR_INVALID.
+ * fp32 data becomes fp16 with the context's conversion (the reference's CopyFromFloat32 bytes
+ * by default).  Synchronous: `data` may be freed on return.  The model can run once every
+ * tensor of Cuda_Model_TensorCount has been loaded (Cuda_Model_IsLoaded). */
+int32_t Cuda_Model_LoadTensor(CudaModelRef model, const char* name, int32_t dtype, const void* data, int64_t rows,
+                              int64_t cols, int32_t transposed);
+/* Number of checkpoint tensors of a config, and the name of tensor `index` in LoadFromSafeTensors
+ * order (loader.go:257-293). */
+int32_t Cuda_Model_TensorCount(const FletcherBertConfig* cfg);
+int32_t Cuda_Model_TensorName(const FletcherBertConfig* cfg, int32_t index, char* buf, int32_t len);
+/* 1 once the model holds a full set of weights (Cuda_Model_LoadRaw, or every LoadTensor). */
+int32_t Cuda_Model_IsLoaded(CudaModelRef model);
 /* BertModel.ForwardBatch(ids, lengths) (bert.go:149): host ids (packed, sum(lengths)
  * entries) and lengths in, host float32 out[numSeqs, hidden].  Synchronous. */
 int32_t Cuda_Model_ForwardBatch(CudaModelRef model, const int32_t* ids, const int32_t* lengths,
                                 int32_t numSeqs, int32_t pooling, float* out);
 /* Cuda_Model_ForwardBatch with the vectors returned as out_dtype (FLETCHER_F32, F16 or BF16;
- * 16-bit values are rounded to nearest-even on the device, so half the bytes cross PCIe): the
- * reference's fp16 transport, Cast(Float16) + ExtractBytes (embeddings.go:256-288). */
+ * converted on the device, so half the bytes cross PCIe; fp16 with the context's conversion,
+ * the reference's bytes by default, bf16 rounded to nearest even): the reference's fp16
+ * transport, Cast(Float16) + ExtractBytes (embeddings.go:256-288). */
 int32_t Cuda_Model_ForwardBatchEx(CudaModelRef model, const int32_t* ids, const int32_t* lengths,
                                   int32_t numSeqs, int32_t pooling, int32_t out_dtype, void* out);
 /* Asynchronous Cuda_Model_ForwardBatchEx for a batcher's double buffering (the reference's

@@ -30,12 +30,60 @@ struct Temp {
   }
 };
 
+// Small per-call host metadata -> a stream-ordered temporary, copied through the context's
+// pinned staging ring (no host synchronisation; the caller may free its array on return).
 int32_t upload(Ctx* c, Temp& t, const void* h, int64_t bytes) {
   int32_t rc = t.alloc(bytes);
   if (rc) return rc;
-  FL_CUDA(c, cudaMemcpyAsync(t.p, h, bytes, cudaMemcpyHostToDevice, c->stream));
-  // The host array may be freed by the caller right after return.
-  FL_CUDA(c, cudaStreamSynchronize(c->stream));
+  return stage_to_device(c, t.p, h, bytes);
+}
+
+// Cuda_Linear_Fused's 16-bit weight in the tensor-core layout (K-major [N', K], SwiGLU
+// interleaved), built once per weight contents and layout and kept with the weight buffer.
+int32_t packed_weight(Ctx* c, Buf* w, int64_t K, int64_t N, bool swiglu, int bn, const void** out) {
+  const int key = (swiglu ? 1 : 0) | (bn << 1);
+  const int64_t bytes = K * N * 2;
+  if (!(w->packed && w->packed_key == key && w->packed_ver == w->version && w->packed_bytes == bytes)) {
+    dev_free(c, w->packed, w->packed_bytes);
+    w->packed = nullptr;
+    w->packed_bytes = 0;
+    int32_t rc = dev_alloc(c, &w->packed, bytes);
+    if (rc) return rc;
+    w->packed_bytes = bytes;
+    if ((rc = launch_pack_kmajor_16(c, w->dtype, w->ptr, K, N, w->packed, swiglu ? 1 : 0, bn))) {
+      w->packed_key = -1;
+      return rc;
+    }
+    w->packed_key = key;
+    w->packed_ver = w->version;
+  }
+  *out = w->packed;
+  return FLETCHER_OK;
+}
+
+// The bias widened to fp32 in the packed column order, cached like the weight.
+int32_t packed_bias(Ctx* c, Buf* b, int64_t N, bool swiglu, int bn, const float** out) {
+  const int key = (swiglu ? 1 : 0) | (bn << 1);
+  if (!(b->bias32 && b->bias32_key == key && b->bias32_ver == b->version && b->bias32_bytes == N * 4)) {
+    dev_free(c, b->bias32, b->bias32_bytes);
+    b->bias32 = nullptr;
+    b->bias32_bytes = 0;
+    int32_t rc = dev_alloc(c, (void**)&b->bias32, N * 4);
+    if (rc) return rc;
+    b->bias32_bytes = N * 4;
+    b->bias32_key = -1;
+    if (swiglu) {  // interleave the bias like the weight rows: pack a [1, N] row as K=1
+      Temp b16(c);
+      if ((rc = b16.alloc(N * 2))) return rc;
+      if ((rc = launch_pack_kmajor_16(c, b->dtype, b->ptr, 1, N, b16.p, 1, bn))) return rc;
+      if ((rc = launch_cast(c, b->dtype, b16.p, FLETCHER_F32, b->bias32, N))) return rc;
+    } else if ((rc = launch_cast(c, b->dtype, b->ptr, FLETCHER_F32, b->bias32, N))) {
+      return rc;
+    }
+    b->bias32_key = key;
+    b->bias32_ver = b->version;
+  }
+  *out = b->bias32;
   return FLETCHER_OK;
 }
 
@@ -59,28 +107,19 @@ int32_t Cuda_Linear_Fused(CudaContextRef ctx, CudaBufferRef input, int64_t rows,
            "Linear: buffer smaller than its shape");
   const int act = (activation == FLETCHER_ACT_GELU || activation == FLETCHER_ACT_TANH) ? activation : FLETCHER_ACT_IDENTITY;
   int32_t rc;
-  // 16-bit: tensor-core GEMM.  The (in,out) weight is packed K-major into a temporary (SwiGLU
-  // weights gate/up-interleaved per tile) and the bias widened to fp32.
+  touch(y);
+  // 16-bit: tensor-core GEMM on the cached K-major packing of the (in,out) weight (SwiGLU
+  // weights gate/up-interleaved per tile) and the cached fp32 bias.
   const int bn = swiglu || (outCols % 256 == 0 && outCols >= 1024) ? 256 : 128;
   const bool tc_act = activation == FLETCHER_ACT_IDENTITY || activation == FLETCHER_ACT_GELU || swiglu;
   if (dt != FLETCHER_F32 && tc_act && gemm_tc_supported(rows, outCols, inCols, bn) && (!swiglu || outCols % bn == 0)) {
-    Temp wk(c), bf(c);
-    if ((rc = wk.alloc(inCols * outCols * 2))) return rc;
-    if ((rc = launch_pack_kmajor_16(c, dt, w->ptr, inCols, outCols, wk.p, swiglu ? 1 : 0, bn))) return rc;
-    if (b) {
-      if ((rc = bf.alloc(outCols * 4))) return rc;
-      if (swiglu) {  // interleave the bias like the weight rows: pack a [1, N] row as K=1
-        Temp b16(c);
-        if ((rc = b16.alloc(outCols * 2))) return rc;
-        if ((rc = launch_pack_kmajor_16(c, dt, b->ptr, 1, outCols, b16.p, 1, bn))) return rc;
-        if ((rc = launch_cast(c, dt, b16.p, FLETCHER_F32, bf.p, outCols))) return rc;
-      } else if ((rc = launch_cast(c, dt, b->ptr, FLETCHER_F32, bf.p, outCols))) {
-        return rc;
-      }
-    }
+    const void* wk = nullptr;
+    const float* bf = nullptr;
+    if ((rc = packed_weight(c, w, inCols, outCols, swiglu, bn, &wk))) return rc;
+    if (b && (rc = packed_bias(c, b, outCols, swiglu, bn, &bf))) return rc;
     const int epi = swiglu ? EPI_SWIGLU : activation == FLETCHER_ACT_GELU ? EPI_GELU : EPI_STORE;
-    return launch_gemm_tc(c, dt, epi, bn, x->ptr, rows, inCols, wk.p, outCols, y->ptr, ycols, b ? (const float*)bf.p : nullptr,
-                          nullptr, 0, nullptr, nullptr, nullptr, 0);
+    return launch_gemm_tc(c, dt, epi, bn, x->ptr, rows, inCols, wk, outCols, y->ptr, ycols, bf, nullptr, 0, nullptr,
+                          nullptr, nullptr, 0);
   }
   if (!swiglu && activation != FLETCHER_ACT_SOFTMAX) {
     rc = launch_gemm_simt(c, dt, x->ptr, inCols, w->ptr, outCols, y->ptr, outCols, rows, outCols, inCols,
@@ -108,6 +147,7 @@ int32_t Cuda_LayerNorm(CudaContextRef ctx, CudaBufferRef input, CudaBufferRef ga
   FL_CHECK(c, ga->dtype == FLETCHER_F32 && be->dtype == FLETCHER_F32, "LayerNorm: gamma/beta must be f32");
   FL_CHECK(c, x->dtype == y->dtype, "LayerNorm: dtype mismatch");
   FL_CHECK(c, fits(x, rows * cols) && fits(y, rows * cols) && fits(ga, cols) && fits(be, cols), "LayerNorm: shape");
+  touch(y);
   return launch_add_layernorm(c, x->dtype, x->ptr, nullptr, y->ptr, (const float*)ga->ptr, (const float*)be->ptr, rows,
                               cols, eps);
 }
@@ -122,6 +162,7 @@ int32_t Cuda_AddLayerNorm(CudaContextRef ctx, CudaBufferRef xb, CudaBufferRef re
   FL_CHECK(c, ga->dtype == FLETCHER_F32 && be->dtype == FLETCHER_F32, "AddLayerNorm: gamma/beta must be f32");
   FL_CHECK(c, x->dtype == r->dtype, "AddLayerNorm: dtype mismatch");
   FL_CHECK(c, fits(x, rows * cols) && fits(r, rows * cols) && fits(ga, cols) && fits(be, cols), "AddLayerNorm: shape");
+  touch(x);
   return launch_add_layernorm(c, x->dtype, x->ptr, r->ptr, x->ptr, (const float*)ga->ptr, (const float*)be->ptr, rows,
                               cols, eps);
 }
@@ -132,6 +173,7 @@ int32_t Cuda_Softmax(CudaContextRef ctx, CudaBufferRef input, CudaBufferRef resu
   DeviceGuard g(c);
   Buf *x = B(input), *y = B(result);
   FL_CHECK(c, x && y && x->dtype == y->dtype && fits(x, rows * cols) && fits(y, rows * cols), "Softmax: bad buffers");
+  touch(y);
   if (x != y)
     FL_CUDA(c, cudaMemcpyAsync(y->ptr, x->ptr, rows * cols * dtype_size(x->dtype), cudaMemcpyDeviceToDevice, c->stream));
   return launch_activation(c, y->dtype, y->ptr, rows, cols, FLETCHER_ACT_SOFTMAX);
@@ -149,6 +191,7 @@ int32_t Cuda_Gather(CudaContextRef ctx, CudaBufferRef table, const int32_t* indi
   for (int64_t i = 0; i < count; i++)  // cpu_backend.go:501-502 panics on a bad index
     FL_CHECK(c, indices[i] >= 0 && indices[i] < rows, "Gather index out of bounds: %d", indices[i]);
   if (count == 0) return FLETCHER_OK;
+  touch(o);
   Temp idx(c);
   int32_t rc = upload(c, idx, indices, count * 4);
   if (rc) return rc;
@@ -167,6 +210,7 @@ int32_t Cuda_Add(CudaContextRef ctx, CudaBufferRef x, CudaBufferRef other, int64
   DeviceGuard g(c);
   Buf *a = B(x), *b = B(other);
   FL_CHECK(c, a && b && a->dtype == b->dtype && fits(a, count) && fits(b, count), "Add: bad buffers");
+  touch(a);
   return launch_scale_add(c, a->dtype, a->ptr, b->ptr, 1.0f, 0.0f, count);
 }
 
@@ -176,6 +220,7 @@ int32_t Cuda_Scale(CudaContextRef ctx, CudaBufferRef x, float val, int64_t count
   DeviceGuard g(c);
   Buf* a = B(x);
   FL_CHECK(c, a && fits(a, count), "Scale: bad buffer");
+  touch(a);
   if (val == 1.0f) return FLETCHER_OK;
   return launch_scale_add(c, a->dtype, a->ptr, nullptr, val, 0.0f, count);
 }
@@ -186,6 +231,7 @@ int32_t Cuda_AddScalar(CudaContextRef ctx, CudaBufferRef x, float val, int64_t c
   DeviceGuard g(c);
   Buf* a = B(x);
   FL_CHECK(c, a && fits(a, count), "AddScalar: bad buffer");
+  touch(a);
   return launch_scale_add(c, a->dtype, a->ptr, nullptr, 1.0f, val, count);
 }
 
@@ -195,6 +241,7 @@ int32_t Cuda_AddBias(CudaContextRef ctx, CudaBufferRef x, CudaBufferRef bias, in
   DeviceGuard g(c);
   Buf *a = B(x), *b = B(bias);
   FL_CHECK(c, a && b && a->dtype == b->dtype && fits(a, rows * cols) && fits(b, cols), "AddBias: bad buffers");
+  touch(a);
   return launch_add_bias(c, a->dtype, a->ptr, b->ptr, rows, cols);
 }
 
@@ -204,6 +251,7 @@ int32_t Cuda_Activation(CudaContextRef ctx, CudaBufferRef x, int64_t rows, int64
   DeviceGuard g(c);
   Buf* a = B(x);
   FL_CHECK(c, a && fits(a, rows * cols), "Activation: bad buffer");
+  touch(a);
   return launch_activation(c, a->dtype, a->ptr, rows, cols, activation);
 }
 
@@ -213,7 +261,8 @@ int32_t Cuda_Cast(CudaContextRef ctx, CudaBufferRef src, CudaBufferRef dst, int6
   DeviceGuard g(c);
   Buf *s = B(src), *d = B(dst);
   FL_CHECK(c, s && d && fits(s, count) && fits(d, count), "Cast: bad buffers");
-  return launch_cast(c, s->dtype, s->ptr, d->dtype, d->ptr, count);
+  touch(d);
+  return launch_cast(c, s->dtype, s->ptr, d->dtype, d->ptr, count, c->half_mode == FLETCHER_HALF_REFERENCE);
 }
 
 int32_t Cuda_HasNaN(CudaContextRef ctx, CudaBufferRef x, int64_t count, int32_t* result) {
@@ -251,6 +300,7 @@ static int32_t attention_common(Ctx* c, Buf* q, Buf* k, Buf* v, Buf* out, const 
   const int32_t dh = (int32_t)(hidden / nh);
   const int32_t Bn = (int32_t)lens.size();
   if (T == 0) return FLETCHER_OK;
+  touch(out);
   std::vector<int32_t> cu(Bn + 1, 0);
   for (int i = 0; i < Bn; i++) cu[i + 1] = cu[i] + lens[i];
   Temp dcu(c);
@@ -297,6 +347,7 @@ static int32_t rope_common(Ctx* c, Buf* x, const std::vector<int32_t>& pos, int3
   FL_CHECK(c, x && nh > 0 && dh > 0 && dh % 2 == 0, "ApplyRoPE: bad arguments");
   FL_CHECK(c, fits(x, T * nh * dh), "ApplyRoPE: buffer smaller than rows*heads*headDim");
   if (T == 0) return FLETCHER_OK;
+  touch(x);
   int32_t mx = 0;
   for (int32_t p : pos) mx = std::max(mx, p);
   Temp dpos(c), tab(c);
@@ -349,10 +400,89 @@ int32_t Cuda_MeanPoolL2(CudaContextRef ctx, CudaBufferRef hidden, const int32_t*
   }
   FL_CHECK(c, fits(h, (int64_t)cu[numSeqs] * cols) && fits(o, (int64_t)numSeqs * cols), "MeanPoolL2: shape");
   if (numSeqs == 0) return FLETCHER_OK;
+  touch(o);
   Temp dcu(c);
   int32_t rc = upload(c, dcu, cu.data(), (numSeqs + 1) * 4);
   if (rc) return rc;
   return launch_mean_pool_l2(c, h->dtype, h->ptr, (const int32_t*)dcu.p, numSeqs, cols, (float*)o->ptr);
+}
+
+int32_t Cuda_Copy(CudaContextRef ctx, CudaBufferRef dst, int64_t dstOffset, CudaBufferRef src, int64_t srcOffset,
+                  int64_t count) {
+  Ctx* c = C(ctx);
+  if (!c) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(c);
+  Buf *d = B(dst), *s = B(src);
+  FL_CHECK(c, d && s, "Copy: null buffer");
+  FL_CHECK(c, dstOffset >= 0 && srcOffset >= 0 && count >= 0 && fits(d, dstOffset + count) && fits(s, srcOffset + count),
+           "Copy: range out of bounds");
+  if (count == 0) return FLETCHER_OK;
+  touch(d);
+  char* dp = (char*)d->ptr + dstOffset * dtype_size(d->dtype);
+  const char* sp = (const char*)s->ptr + srcOffset * dtype_size(s->dtype);
+  if (d->dtype == s->dtype) {
+    FL_CUDA(c, cudaMemcpyAsync(dp, sp, count * dtype_size(d->dtype), cudaMemcpyDeviceToDevice, c->stream));
+    return FLETCHER_OK;
+  }
+  return launch_cast(c, s->dtype, sp, d->dtype, dp, count, c->half_mode == FLETCHER_HALF_REFERENCE);
+}
+
+int32_t Cuda_Slice(CudaContextRef ctx, CudaBufferRef src, int64_t i, int64_t k, int64_t j, int64_t l,
+                   CudaBufferRef dst) {
+  Ctx* c = C(ctx);
+  if (!c) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(c);
+  Buf *s = B(src), *d = B(dst);
+  FL_CHECK(c, s && d, "Slice: null buffer");
+  FL_CHECK(c, k > i && l > j, "Slice: invalid dimensions");  // cpu_backend.go:292-294
+  FL_CHECK(c, i >= 0 && j >= 0 && k <= s->rows && l <= s->cols, "Slice [%lld:%lld, %lld:%lld] outside a %lldx%lld tensor",
+           (long long)i, (long long)k, (long long)j, (long long)l, (long long)s->rows, (long long)s->cols);
+  FL_CHECK(c, d->dtype == s->dtype && fits(d, (k - i) * (l - j)), "Slice: destination must hold %lldx%lld of the source dtype",
+           (long long)(k - i), (long long)(l - j));
+  touch(d);
+  const int64_t es = dtype_size(s->dtype);
+  FL_CUDA(c, cudaMemcpy2DAsync(d->ptr, (size_t)((l - j) * es), (const char*)s->ptr + (i * s->cols + j) * es,
+                               (size_t)(s->cols * es), (size_t)((l - j) * es), (size_t)(k - i), cudaMemcpyDeviceToDevice,
+                               c->stream));
+  return FLETCHER_OK;
+}
+
+int32_t Cuda_Mul(CudaContextRef ctx, CudaBufferRef a, int32_t transA, CudaBufferRef b, int32_t transB, CudaBufferRef cb,
+                 int64_t m, int64_t n, int64_t k) {
+  Ctx* c = C(ctx);
+  if (!c) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(c);
+  Buf *A = B(a), *Bm = B(b), *Cm = B(cb);
+  FL_CHECK(c, A && Bm && Cm, "Mul: null buffer");
+  FL_CHECK(c, m >= 0 && n >= 0 && k >= 0, "Mul: negative shape");
+  const int32_t dt = Cm->dtype;
+  FL_CHECK(c, A->dtype == dt && Bm->dtype == dt, "Mul: dtype mismatch");
+  FL_CHECK(c, fits(A, m * k) && fits(Bm, k * n) && fits(Cm, m * n), "Mul: buffers smaller than %lldx%lld . %lldx%lld",
+           (long long)m, (long long)k, (long long)k, (long long)n);
+  if (m == 0 || n == 0) return FLETCHER_OK;
+  touch(Cm);
+  if (k == 0) {  // beta = 0: an empty product is zero
+    FL_CUDA(c, cudaMemsetAsync(Cm->ptr, 0, m * n * dtype_size(dt), c->stream));
+    return FLETCHER_OK;
+  }
+  // 16-bit, A not transposed: tensor cores.  B^T stored [n, k] is already the K-major operand;
+  // a plain B [k, n] is packed K-major into a temporary first.
+  if (dt != FLETCHER_F32 && !transA && gemm_tc_supported(m, n, k, 128) &&
+      ((uintptr_t)A->ptr & 15) == 0 && ((uintptr_t)Bm->ptr & 15) == 0 && n % 8 == 0) {
+    if (transB) return launch_gemm_tc(c, dt, EPI_STORE, 128, A->ptr, m, k, Bm->ptr, n, Cm->ptr, n, nullptr, nullptr, 0,
+                                      nullptr, nullptr, nullptr, 0);
+    Temp wk(c);
+    int32_t rc = wk.alloc(k * n * 2);
+    if (rc) return rc;
+    if ((rc = launch_pack_kmajor_16(c, dt, Bm->ptr, k, n, wk.p, 0, 0))) return rc;
+    return launch_gemm_tc(c, dt, EPI_STORE, 128, A->ptr, m, k, wk.p, n, Cm->ptr, n, nullptr, nullptr, 0, nullptr,
+                          nullptr, nullptr, 0);
+  }
+  // SIMT (fp32 accumulation; the fp32 parity path): strides express the T() views.
+  const int64_t sam = transA ? 1 : k, sak = transA ? m : 1;
+  const int64_t sbk = transB ? 1 : n, sbn = transB ? k : 1;
+  return launch_gemm_simt_strided(c, dt, A->ptr, sam, sak, Bm->ptr, sbk, sbn, Cm->ptr, n, m, n, k, nullptr,
+                                  FLETCHER_ACT_IDENTITY);
 }
 
 }  // extern "C"

@@ -8,6 +8,8 @@
 //
 // k_attn_f32: one CTA per (query row, head); scores in shared memory, the reference's ExpFast
 // softmax (max, ExpFast(s-max), sum, * 1/sum) then P.V.
+#include <atomic>
+
 #include "kernels.cuh"
 
 namespace fl {
@@ -92,7 +94,13 @@ int32_t launch_attention_f32(Ctx* c, const float* q, const float* k, const float
   const int G = 128 / dh > 0 ? 128 / dh : 1;
   const size_t smem = (size_t)(dh + max_len + G * (dh < 128 ? dh : 128)) * 4;
   FL_CHECK(c, smem <= 200 * 1024, "attention_f32: sequence length %d too long for the fp32 kernel", max_len);
-  if (smem > 48 * 1024) FL_CUDA(c, cudaFuncSetAttribute(k_attn_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // The attribute is per device; set it once to the cap checked above, so that replica threads
+  // sharing a GPU never lower it between another thread's set and launch.
+  static std::atomic<bool> attr_set[64] = {};
+  if (smem > 48 * 1024 && c->device < 64 && !attr_set[c->device].load(std::memory_order_acquire)) {
+    FL_CUDA(c, cudaFuncSetAttribute(k_attn_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr_set[c->device].store(true, std::memory_order_release);
+  }
   dim3 grid((unsigned)T, (unsigned)nh);
   k_attn_f32<<<grid, 128, smem, c->stream>>>(q, k, v, ld_in, out, ld_out, cu, B, dh, scale);
   FL_LAUNCH(c);

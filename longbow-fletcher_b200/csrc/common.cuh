@@ -26,6 +26,15 @@ struct Ctx {
   int64_t launches = 0;      // kernels launched on this context (counted by FL_LAUNCH)
   float* splitk = nullptr;   // split-K workspace of small-M GEMMs, lent by the running model
   int64_t splitk_bytes = 0;
+  int32_t half_mode = FLETCHER_HALF_REFERENCE;  // fp32 <-> fp16 conversion of host-facing copies
+  // Pinned staging ring for small per-call host arrays (lengths, indices): a slot is reused
+  // once the copy that last read it has completed (its event), so calls never block on the
+  // stream the way a synchronous upload would.
+  static constexpr int kStageSlots = 8;
+  uint8_t* h_stage[kStageSlots] = {};
+  int64_t h_stage_cap[kStageSlots] = {};
+  cudaEvent_t stage_ev[kStageSlots] = {};
+  int stage_next = 0;
   std::string last_error;
 };
 
@@ -35,7 +44,29 @@ struct Buf {
   int64_t bytes = 0;
   int64_t rows = 0, cols = 0;
   int32_t dtype = FLETCHER_F32;
+  // Write counter: bumped by every ABI call that may change the contents (see touch()).
+  uint64_t version = 0;
+  // Cuda_Linear_Fused's derived copies of a 16-bit weight / bias, valid while `version` equals
+  // the recorded one and the layout key (SwiGLU interleave, tile width) matches.
+  void* packed = nullptr;
+  int64_t packed_bytes = 0;
+  int packed_key = -1;
+  uint64_t packed_ver = 0;
+  float* bias32 = nullptr;
+  int64_t bias32_bytes = 0;
+  int bias32_key = -1;
+  uint64_t bias32_ver = 0;
 };
+
+// Marks a buffer as written (invalidates Cuda_Linear_Fused's cached layouts of it).
+inline void touch(Buf* b) {
+  if (b) b->version++;
+}
+
+// Copies `bytes` of host memory to device memory `d` in stream order through the context's
+// pinned staging ring; the host array may be reused as soon as this returns.
+int32_t stage_to_device(Ctx* c, void* d, const void* h, int64_t bytes);
+void free_staging(Ctx* c);
 
 inline int64_t dtype_size(int32_t dt) { return dt == FLETCHER_F32 ? 4 : 2; }
 
@@ -105,6 +136,43 @@ template <typename T> __device__ __forceinline__ T from_f(float v);
 template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
+// The reference's host-side fp16 conversion (internal/device/utils.go:13-72), which its fp16 CUDA
+// backend applies to every CopyFromFloat32 / Set / ToHost (cuda_linux.go:128,148,163): NaN ->
+// 0x7E00; +-Inf kept; finite values clamped to +-65504; |x| below the smallest normal (2^-14)
+// flushed to a signed zero; otherwise the mantissa is truncated (not rounded) to 10 bits.
+__device__ __forceinline__ uint16_t half_bits_ref(float f) {
+  if (f != f) return 0x7E00;
+  if (isinf(f)) return f > 0.0f ? 0x7C00 : 0xFC00;
+  f = fminf(fmaxf(f, -65504.0f), 65504.0f);
+  const float a = fabsf(f);
+  if (a < 6.103515625e-05f && a > 0.0f) return f < 0.0f ? 0x8000 : 0x0000;
+  const uint32_t bits = __float_as_uint(f);
+  const uint32_t sign = (bits >> 16) & 0x8000u;
+  const int e = (int)((bits >> 23) & 0xFF) - 127 + 15;
+  const uint32_t frac = (bits >> 13) & 0x3FFu;
+  if (e >= 0x1F) return (uint16_t)(sign | 0x7BFFu);
+  if (e <= 0) return (uint16_t)sign;
+  return (uint16_t)(sign | ((uint32_t)e << 10) | frac);
+}
+// Float16ToFloat32 (utils.go:75-91): zero and every subnormal read as +0; Inf/NaN keep their
+// payload; normals widen exactly.
+__device__ __forceinline__ float half_bits_to_f32_ref(uint16_t h) {
+  const uint32_t sign = (h >> 15) & 1u, e = (h >> 10) & 0x1Fu, frac = h & 0x3FFu;
+  if (e == 0) return 0.0f;
+  if (e == 31) return __uint_as_float((sign << 31) | (0xFFu << 23) | (frac << 13));
+  return __uint_as_float((sign << 31) | ((e - 15 + 127) << 23) | (frac << 13));
+}
+// Host-facing conversions: fp16 follows the context's mode (the reference's bytes, or IEEE
+// round-to-nearest-even); bf16 and fp32 are unaffected.
+template <typename T> __device__ __forceinline__ T from_f_host(float v, bool ref) { return from_f<T>(v); }
+template <> __device__ __forceinline__ __half from_f_host<__half>(float v, bool ref) {
+  return ref ? __ushort_as_half(half_bits_ref(v)) : __float2half_rn(v);
+}
+template <typename T> __device__ __forceinline__ float to_f_host(T v, bool ref) { return to_f<T>(v); }
+template <> __device__ __forceinline__ float to_f_host<__half>(__half v, bool ref) {
+  return ref ? half_bits_to_f32_ref(__half_as_ushort(v)) : __half2float(v);
+}
 
 // The reference's fast-math helpers (internal/simd/simd.go), written with explicitly
 // rounded float operations so that the compiler cannot contract them into FMAs: the

@@ -2,7 +2,10 @@
 // Replaces Cuda_Init / Cuda_Alloc / Cuda_Copy* of the reference (cuda_backend.cu:17-63),
 // which bound the device only once and used synchronous cudaMalloc/cudaMemcpy.
 #include <cstdarg>
+#include <cmath>
 #include <cstring>
+
+#include <algorithm>
 
 #include "common.cuh"
 
@@ -58,19 +61,53 @@ static int32_t init_on_device(Ctx* c, int device) {
   return FLETCHER_OK;
 }
 
+// ---- host-side scalar conversions for Cuda_At / Cuda_Set (one element, no kernel).
+// The reference's Float32ToFloat16 (utils.go:13-72); same steps as half_bits_ref on the device.
+static uint16_t host_f32_to_half_ref(float f) {
+  if (std::isnan(f)) return 0x7E00;
+  if (std::isinf(f)) return f > 0 ? 0x7C00 : 0xFC00;
+  if (f > 65504.0f) f = 65504.0f;
+  else if (f < -65504.0f) f = -65504.0f;
+  const float a = std::fabs(f);
+  if (a < 6.103515625e-05f && a > 0.0f) return f < 0 ? 0x8000 : 0x0000;
+  uint32_t bits;
+  memcpy(&bits, &f, 4);
+  const uint32_t sign = (bits >> 16) & 0x8000u;
+  const int e = (int)((bits >> 23) & 0xFF) - 127 + 15;
+  const uint32_t frac = (bits >> 13) & 0x3FFu;
+  if (e >= 0x1F) return (uint16_t)(sign | 0x7BFFu);
+  if (e <= 0) return (uint16_t)sign;
+  return (uint16_t)(sign | ((uint32_t)e << 10) | frac);
+}
+// Float16ToFloat32 (utils.go:75-91).
+static float host_half_to_f32_ref(uint16_t h) {
+  const uint32_t sign = (h >> 15) & 1u, e = (h >> 10) & 0x1Fu, frac = h & 0x3FFu;
+  if (e == 0) return 0.0f;
+  uint32_t bits = e == 31 ? (sign << 31) | (0xFFu << 23) | (frac << 13)
+                          : (sign << 31) | ((e - 15 + 127) << 23) | (frac << 13);
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+// IEEE conversions (FLETCHER_HALF_RNE, bf16): cuda_fp16.h / cuda_bf16.h are host-callable.
+static uint16_t host_f32_to_half_rne(float f) { return __half_as_ushort(__float2half_rn(f)); }
+static float host_half_to_f32_ieee(uint16_t r) { return __half2float(__ushort_as_half(r)); }
+static uint32_t host_f32_to_bf16_rne(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+
 static Ctx* C(CudaContextRef r) { return reinterpret_cast<Ctx*>(r); }
 static Buf* B(CudaBufferRef r) { return reinterpret_cast<Buf*>(r); }
 
 // Converts a float32 staging buffer into dst's dtype.
+// fp16 follows the context's conversion mode (ref = the reference's utils.go bytes).
 template <typename T>
-__global__ void k_from_f32(const float* __restrict__ s, T* __restrict__ d, int64_t n) {
+__global__ void k_from_f32(const float* __restrict__ s, T* __restrict__ d, int64_t n, bool ref) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    d[i] = from_f<T>(s[i]);
+    d[i] = from_f_host<T>(s[i], ref);
 }
 template <typename T>
-__global__ void k_to_f32(const T* __restrict__ s, float* __restrict__ d, int64_t n) {
+__global__ void k_to_f32(const T* __restrict__ s, float* __restrict__ d, int64_t n, bool ref) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    d[i] = to_f<T>(s[i]);
+    d[i] = to_f_host<T>(s[i], ref);
 }
 
 int32_t convert_from_f32(Ctx* c, const float* src, void* dst, int32_t dtype, int64_t n) {
@@ -79,9 +116,9 @@ int32_t convert_from_f32(Ctx* c, const float* src, void* dst, int32_t dtype, int
   if (dtype == FLETCHER_F32)
     FL_CUDA(c, cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, c->stream));
   else if (dtype == FLETCHER_BF16)
-    k_from_f32<__nv_bfloat16><<<blocks, 256, 0, c->stream>>>(src, (__nv_bfloat16*)dst, n);
+    k_from_f32<__nv_bfloat16><<<blocks, 256, 0, c->stream>>>(src, (__nv_bfloat16*)dst, n, false);
   else
-    k_from_f32<__half><<<blocks, 256, 0, c->stream>>>(src, (__half*)dst, n);
+    k_from_f32<__half><<<blocks, 256, 0, c->stream>>>(src, (__half*)dst, n, c->half_mode == FLETCHER_HALF_REFERENCE);
   FL_LAUNCH(c);
   return FLETCHER_OK;
 }
@@ -92,11 +129,43 @@ int32_t convert_to_f32(Ctx* c, const void* src, int32_t dtype, float* dst, int64
   if (dtype == FLETCHER_F32)
     FL_CUDA(c, cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, c->stream));
   else if (dtype == FLETCHER_BF16)
-    k_to_f32<__nv_bfloat16><<<blocks, 256, 0, c->stream>>>((const __nv_bfloat16*)src, dst, n);
+    k_to_f32<__nv_bfloat16><<<blocks, 256, 0, c->stream>>>((const __nv_bfloat16*)src, dst, n, false);
   else
-    k_to_f32<__half><<<blocks, 256, 0, c->stream>>>((const __half*)src, dst, n);
+    k_to_f32<__half><<<blocks, 256, 0, c->stream>>>((const __half*)src, dst, n, c->half_mode == FLETCHER_HALF_REFERENCE);
   FL_LAUNCH(c);
   return FLETCHER_OK;
+}
+
+int32_t stage_to_device(Ctx* c, void* d, const void* h, int64_t bytes) {
+  if (bytes <= 0) return FLETCHER_OK;
+  const int i = c->stage_next;
+  c->stage_next = (i + 1) % Ctx::kStageSlots;
+  if (!c->stage_ev[i]) FL_CUDA(c, cudaEventCreateWithFlags(&c->stage_ev[i], cudaEventDisableTiming));
+  else FL_CUDA(c, cudaEventSynchronize(c->stage_ev[i]));  // this slot's previous copy has read it
+  if (bytes > c->h_stage_cap[i]) {
+    if (c->h_stage[i]) cudaFreeHost(c->h_stage[i]);
+    c->h_stage[i] = nullptr;
+    c->h_stage_cap[i] = 0;
+    const int64_t cap = std::max<int64_t>(bytes * 2, 1 << 16);
+    FL_CUDA(c, cudaHostAlloc((void**)&c->h_stage[i], (size_t)cap, cudaHostAllocPortable));
+    c->h_stage_cap[i] = cap;
+  }
+  memcpy(c->h_stage[i], h, (size_t)bytes);
+  FL_CUDA(c, cudaMemcpyAsync(d, c->h_stage[i], (size_t)bytes, cudaMemcpyHostToDevice, c->stream));
+  FL_CUDA(c, cudaEventRecord(c->stage_ev[i], c->stream));
+  return FLETCHER_OK;
+}
+
+// Frees the staging ring (after the stream has drained).
+void free_staging(Ctx* c) {
+  for (int i = 0; i < Ctx::kStageSlots; i++) {
+    if (c->h_stage[i]) cudaFreeHost(c->h_stage[i]);
+    if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);
+    c->h_stage[i] = nullptr;
+    c->h_stage_cap[i] = 0;
+    c->stage_ev[i] = nullptr;
+  }
+  c->stage_next = 0;
 }
 
 // Reads and clears the device error flag (after the stream has been synchronised).
@@ -150,6 +219,7 @@ int32_t Cuda_SetDevice(CudaContextRef ctx, int32_t device) {
   {
     DeviceGuard g(c);
     cudaStreamSynchronize(c->stream);
+    free_staging(c);  // the ring's events belong to the old device
     cudaFree(c->d_err);
     cudaStreamDestroy(c->stream);
   }
@@ -162,6 +232,7 @@ void Cuda_FreeContext(CudaContextRef ctx) {
   if (!c) return;
   DeviceGuard g(c);
   cudaStreamSynchronize(c->stream);
+  free_staging(c);
   cudaFree(c->d_err);
   cudaStreamDestroy(c->stream);
   delete c;
@@ -247,6 +318,8 @@ int32_t Cuda_FreeBuffer(CudaContextRef ctx, CudaBufferRef buf) {
   Ctx* c = ctx ? C(ctx) : b->ctx;
   DeviceGuard g(c);
   dev_free(c, b->ptr, b->bytes);
+  dev_free(c, b->packed, b->packed_bytes);
+  dev_free(c, b->bias32, b->bias32_bytes);
   delete b;
   return FLETCHER_OK;
 }
@@ -257,6 +330,7 @@ int32_t Cuda_CopyToDevice(CudaBufferRef buf, int64_t offset, const void* data, i
   Ctx* c = b->ctx;
   DeviceGuard g(c);
   FL_CHECK(c, offset >= 0 && size >= 0 && offset + size <= b->bytes, "CopyToDevice: range out of bounds");
+  touch(b);
   FL_CUDA(c, cudaMemcpyAsync((char*)b->ptr + offset, data, size, cudaMemcpyHostToDevice, c->stream));
   FL_CUDA(c, cudaStreamSynchronize(c->stream));
   return FLETCHER_OK;
@@ -273,7 +347,13 @@ int32_t Cuda_CopyToHost(CudaBufferRef buf, int64_t offset, void* data, int64_t s
   return FLETCHER_OK;
 }
 
-void* Cuda_GetBufferContents(CudaBufferRef buf) { return buf ? B(buf)->ptr : nullptr; }
+// Handing out the raw pointer counts as a write: the caller may change the contents behind
+// the ABI's back.
+void* Cuda_GetBufferContents(CudaBufferRef buf) {
+  if (!buf) return nullptr;
+  touch(B(buf));
+  return B(buf)->ptr;
+}
 
 int32_t Cuda_BufferInfo(CudaBufferRef buf, int64_t* rows, int64_t* cols, int32_t* dtype) {
   Buf* b = B(buf);
@@ -290,6 +370,7 @@ int32_t Cuda_CopyFromFloat32(CudaBufferRef buf, const float* data, int64_t count
   Ctx* c = b->ctx;
   DeviceGuard g(c);
   FL_CHECK(c, count >= 0 && count * dtype_size(b->dtype) <= b->bytes, "CopyFromFloat32: %lld elements exceed the buffer", (long long)count);
+  touch(b);
   if (b->dtype == FLETCHER_F32) {
     FL_CUDA(c, cudaMemcpyAsync(b->ptr, data, count * 4, cudaMemcpyHostToDevice, c->stream));
   } else {
@@ -322,6 +403,54 @@ int32_t Cuda_ToHostFloat32(CudaBufferRef buf, float* data, int64_t count) {
     FL_CUDA(c, cudaMemcpyAsync(data, stage, count * 4, cudaMemcpyDeviceToHost, c->stream));
     dev_free(c, stage, count * 4);
   }
+  FL_CUDA(c, cudaStreamSynchronize(c->stream));
+  return FLETCHER_OK;
+}
+
+int32_t Cuda_SetHalfConversion(CudaContextRef ctx, int32_t mode) {
+  Ctx* c = C(ctx);
+  if (!c) return FLETCHER_ERR_INVALID;
+  FL_CHECK(c, mode == FLETCHER_HALF_REFERENCE || mode == FLETCHER_HALF_RNE, "SetHalfConversion: unknown mode %d", mode);
+  c->half_mode = mode;
+  return FLETCHER_OK;
+}
+
+int32_t Cuda_At(CudaBufferRef buf, int64_t row, int64_t col, float* value) {
+  Buf* b = B(buf);
+  if (!b || !value) return FLETCHER_ERR_INVALID;
+  Ctx* c = b->ctx;
+  DeviceGuard g(c);
+  FL_CHECK(c, row >= 0 && row < b->rows && col >= 0 && col < b->cols, "At(%lld, %lld) outside a %lldx%lld tensor",
+           (long long)row, (long long)col, (long long)b->rows, (long long)b->cols);
+  const int64_t off = (row * b->cols + col) * dtype_size(b->dtype);
+  uint32_t raw = 0;
+  FL_CUDA(c, cudaMemcpyAsync(&raw, (char*)b->ptr + off, dtype_size(b->dtype), cudaMemcpyDeviceToHost, c->stream));
+  FL_CUDA(c, cudaStreamSynchronize(c->stream));
+  if (b->dtype == FLETCHER_F32) memcpy(value, &raw, 4);
+  else if (b->dtype == FLETCHER_BF16) {
+    const uint32_t w = raw << 16;
+    memcpy(value, &w, 4);
+  } else {
+    *value = c->half_mode == FLETCHER_HALF_REFERENCE ? host_half_to_f32_ref((uint16_t)raw)
+                                                     : host_half_to_f32_ieee((uint16_t)raw);
+  }
+  return FLETCHER_OK;
+}
+
+int32_t Cuda_Set(CudaBufferRef buf, int64_t row, int64_t col, float value) {
+  Buf* b = B(buf);
+  if (!b) return FLETCHER_ERR_INVALID;
+  Ctx* c = b->ctx;
+  DeviceGuard g(c);
+  FL_CHECK(c, row >= 0 && row < b->rows && col >= 0 && col < b->cols, "Set(%lld, %lld) outside a %lldx%lld tensor",
+           (long long)row, (long long)col, (long long)b->rows, (long long)b->cols);
+  touch(b);
+  const int64_t off = (row * b->cols + col) * dtype_size(b->dtype);
+  uint32_t raw = 0;
+  if (b->dtype == FLETCHER_F32) memcpy(&raw, &value, 4);
+  else if (b->dtype == FLETCHER_BF16) raw = host_f32_to_bf16_rne(value);
+  else raw = c->half_mode == FLETCHER_HALF_REFERENCE ? host_f32_to_half_ref(value) : host_f32_to_half_rne(value);
+  FL_CUDA(c, cudaMemcpyAsync((char*)b->ptr + off, &raw, dtype_size(b->dtype), cudaMemcpyHostToDevice, c->stream));
   FL_CUDA(c, cudaStreamSynchronize(c->stream));
   return FLETCHER_OK;
 }

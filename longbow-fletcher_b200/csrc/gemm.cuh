@@ -51,4 +51,9 @@ int32_t launch_gemm_tc(Ctx* c, int32_t dtype, int epi, int bn, const void* A, in
 int32_t launch_gemm_simt(Ctx* c, int32_t dtype, const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
                          int64_t ldc, int64_t M, int64_t N, int64_t K, const void* bias, int32_t act);
 
+// The same with element strides: A(m, k) = A[m*sam + k*sak], B(k, n) = B[k*sbk + n*sbn].
+int32_t launch_gemm_simt_strided(Ctx* c, int32_t dtype, const void* A, int64_t sam, int64_t sak, const void* B,
+                                 int64_t sbk, int64_t sbn, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                 const void* bias, int32_t act);
+
 }  // namespace fl

@@ -9,10 +9,13 @@ namespace fl {
 namespace {
 constexpr int TM = 128, TN = 128, TK = 8;
 
+// A(m, k) = A[m*sam + k*sak] and B(k, n) = B[k*sbk + n*sbn]: unit inner strides for the
+// row-major Linear, swapped ones for Mul's transposed views.
 template <typename T>
-__global__ void __launch_bounds__(256) k_sgemm(const T* __restrict__ A, int64_t lda, const T* __restrict__ B,
-                                               int64_t ldb, T* __restrict__ C, int64_t ldc, int64_t M, int64_t N,
-                                               int64_t K, const T* __restrict__ bias, int act) {
+__global__ void __launch_bounds__(256) k_sgemm(const T* __restrict__ A, int64_t sam, int64_t sak,
+                                               const T* __restrict__ B, int64_t sbk, int64_t sbn, T* __restrict__ C,
+                                               int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                               const T* __restrict__ bias, int act) {
   __shared__ __align__(16) float As[TK][TM];
   __shared__ __align__(16) float Bs[TK][TN];
   const int tid = threadIdx.x;
@@ -30,10 +33,10 @@ __global__ void __launch_bounds__(256) k_sgemm(const T* __restrict__ A, int64_t 
       const int idx = tid * 4 + i;
       const int r = idx / TK, cc = idx % TK;
       const int64_t gm = m0 + r, gk = k0 + cc;
-      As[cc][r] = (gm < M && gk < K) ? to_f<T>(A[gm * lda + gk]) : 0.f;
+      As[cc][r] = (gm < M && gk < K) ? to_f<T>(A[gm * sam + gk * sak]) : 0.f;
       const int br = idx / TN, bc = idx % TN;
       const int64_t bk = k0 + br, bn = n0 + bc;
-      Bs[br][bc] = (bk < K && bn < N) ? to_f<T>(B[bk * ldb + bn]) : 0.f;
+      Bs[br][bc] = (bk < K && bn < N) ? to_f<T>(B[bk * sbk + bn * sbn]) : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -72,22 +75,29 @@ __global__ void __launch_bounds__(256) k_sgemm(const T* __restrict__ A, int64_t 
 }
 }  // namespace
 
-int32_t launch_gemm_simt(Ctx* c, int32_t dt, const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
-                         int64_t ldc, int64_t M, int64_t N, int64_t K, const void* bias, int32_t act) {
+int32_t launch_gemm_simt_strided(Ctx* c, int32_t dt, const void* A, int64_t sam, int64_t sak, const void* B,
+                                 int64_t sbk, int64_t sbn, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                 const void* bias, int32_t act) {
   if (M <= 0 || N <= 0) return FLETCHER_OK;
   FL_CHECK(c, (N + TN - 1) / TN < 65536 * 1024 && (M + TM - 1) / TM < 65536, "gemm_simt: shape too large");
   dim3 grid((unsigned)((N + TN - 1) / TN), (unsigned)((M + TM - 1) / TM));
   if (dt == FLETCHER_F32)
-    k_sgemm<float><<<grid, 256, 0, c->stream>>>((const float*)A, lda, (const float*)B, ldb, (float*)C, ldc, M, N, K,
-                                                (const float*)bias, act);
+    k_sgemm<float><<<grid, 256, 0, c->stream>>>((const float*)A, sam, sak, (const float*)B, sbk, sbn, (float*)C, ldc,
+                                                M, N, K, (const float*)bias, act);
   else if (dt == FLETCHER_BF16)
-    k_sgemm<__nv_bfloat16><<<grid, 256, 0, c->stream>>>((const __nv_bfloat16*)A, lda, (const __nv_bfloat16*)B, ldb,
-                                                        (__nv_bfloat16*)C, ldc, M, N, K, (const __nv_bfloat16*)bias, act);
+    k_sgemm<__nv_bfloat16><<<grid, 256, 0, c->stream>>>((const __nv_bfloat16*)A, sam, sak, (const __nv_bfloat16*)B,
+                                                        sbk, sbn, (__nv_bfloat16*)C, ldc, M, N, K,
+                                                        (const __nv_bfloat16*)bias, act);
   else
-    k_sgemm<__half><<<grid, 256, 0, c->stream>>>((const __half*)A, lda, (const __half*)B, ldb, (__half*)C, ldc, M, N, K,
-                                                 (const __half*)bias, act);
+    k_sgemm<__half><<<grid, 256, 0, c->stream>>>((const __half*)A, sam, sak, (const __half*)B, sbk, sbn, (__half*)C,
+                                                 ldc, M, N, K, (const __half*)bias, act);
   FL_LAUNCH(c);
   return FLETCHER_OK;
+}
+
+int32_t launch_gemm_simt(Ctx* c, int32_t dt, const void* A, int64_t lda, const void* B, int64_t ldb, void* C,
+                         int64_t ldc, int64_t M, int64_t N, int64_t K, const void* bias, int32_t act) {
+  return launch_gemm_simt_strided(c, dt, A, lda, 1, B, ldb, 1, C, ldc, M, N, K, bias, act);
 }
 
 // Kept for callers that only deal in fp32.

@@ -256,13 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*abort && crank == 0)
         for (int s = 0; s < C::STAGES; s++)
           if ((issued >> s) & 1) mbar_drain(&full[s], (issued_par >> s) & 1);
-      // The odd CTA cannot see its loads complete (they signal the even CTA's barriers): it
-      // holds back from the final cluster barrier for ~100 us, far beyond a load's latency.
-      if (*abort && crank != 0 && issued) {
-        const long long t0 = clock64();
-        while (clock64() - t0 < 200000) {
-        }
-      }
+      // The odd CTA cannot see its own loads complete (they signal the even CTA's barriers).
+      // It needs no wait of its own: the even CTA's producer drains both CTAs' loads above
+      // before its threads reach the final cluster barrier, and the odd CTA cannot pass that
+      // barrier (or free anything) until they do.
     }
   } else if (warp == 1) {
     if (lane == 0 && crank == 0) {

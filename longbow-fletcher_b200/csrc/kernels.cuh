@@ -73,9 +73,12 @@ int32_t launch_scale_add(Ctx* c, int32_t dtype, void* x, const void* other, floa
 int32_t launch_add_bias(Ctx* c, int32_t dtype, void* x, const void* bias, int64_t rows, int64_t cols);
 int32_t launch_activation(Ctx* c, int32_t dtype, void* x, int64_t rows, int64_t cols, int32_t act);
 int32_t launch_has_nan(Ctx* c, int32_t dtype, const void* x, int64_t n, int32_t* d_flag);
-int32_t launch_cast(Ctx* c, int32_t sdt, const void* s, int32_t ddt, void* d, int64_t n);
+// ref: use the reference's fp16 conversion (pass ctx->half_mode == FLETCHER_HALF_REFERENCE for
+// host-facing casts); internal casts round to nearest even.
+int32_t launch_cast(Ctx* c, int32_t sdt, const void* s, int32_t ddt, void* d, int64_t n, bool ref = false);
 
-// Weight packing: dst[n', k] (row-major, K contiguous) = src[k, perm(n')] for fp32 src (in,out).
+// Weight packing: dst[n', k] (row-major, K contiguous) = src[k, perm(n')] for fp32 src (in,out);
+// an fp16 destination uses the context's host conversion mode.
 // perm: 0 identity; 1 = SwiGLU interleave of 128-column gate/up blocks (see gemm_tc.cu).
 int32_t launch_pack_weight_kmajor(Ctx* c, const float* src, int64_t K, int64_t N, void* dst,
                                   int32_t dtype, int32_t perm, int32_t block_n);
@@ -83,5 +86,11 @@ int32_t launch_pack_weight_kmajor(Ctx* c, const float* src, int64_t K, int64_t N
 // Same packing from a 16-bit (in,out) [K, N] matrix of dtype dt into K-major [N', K].
 int32_t launch_pack_kmajor_16(Ctx* c, int32_t dt, const void* src, int64_t K, int64_t N, void* dst, int32_t perm,
                               int32_t block_n);
+
+// One checkpoint weight (in,out) [K, N] (src_t = 1: stored (out,in)) of dtype sdt into a model
+// buffer of dtype ddt: K-major rows at row offset `off` with permutation perm (dst_kmajor = 1),
+// or (in,out) with row stride ld at column offset `off`.
+int32_t launch_place_weight(Ctx* c, int32_t sdt, const void* src, int64_t K, int64_t N, int src_t, int32_t ddt,
+                            void* dst, int dst_kmajor, int64_t ld, int64_t off, int perm, int block_n);
 
 }  // namespace fl

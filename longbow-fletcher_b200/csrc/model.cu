@@ -44,6 +44,7 @@ struct Model {
   int64_t H = 0, I = 0, Iup = 0, nh = 0, dh = 0;
   int bn_qkv = 256, bn_o = 128, bn_up = 256, bn_d = 128;
   std::vector<std::pair<void*, int64_t>> allocs;  // everything owned, freed at destroy
+  std::vector<uint8_t> tensor_loaded;              // Cuda_Model_LoadTensor: which checkpoint tensors arrived
   void* word = nullptr;
   void* ptab = nullptr;
   void* type0 = nullptr;
@@ -228,11 +229,26 @@ static int32_t up_table(Model* m, void** d, const float* h, int64_t n, float* st
   return FLETCHER_OK;
 }
 
+// Frees every weight buffer (a second LoadRaw, or LoadRaw after LoadTensor, starts afresh).
+static void release_weights(Model* m) {
+  cudaStreamSynchronize(m->c->stream);
+  clear_graphs(m);  // captured graphs hold the old weight pointers
+  for (auto& a : m->allocs) dev_free(m->c, a.first, a.second);
+  m->allocs.clear();
+  m->word = m->ptab = m->type0 = nullptr;
+  m->eln_g = m->eln_b = nullptr;
+  m->layers.clear();
+  m->wp = m->bp = nullptr;
+  m->loaded = false;
+  m->tensor_loaded.clear();
+}
+
 static int32_t load_raw(Model* m, const float* blob, int64_t count) {
   Ctx* c = m->c;
   const FletcherBertConfig& cf = m->cfg;
   FL_CHECK(c, count == weight_count(&cf), "LoadRaw: %lld values, expected %lld", (long long)count,
            (long long)weight_count(&cf));
+  release_weights(m);
   const int64_t H = m->H, I = m->I, Iup = m->Iup;
   const float* p = blob;
   auto take = [&](int64_t n) {
@@ -319,6 +335,193 @@ static int32_t load_raw(Model* m, const float* blob, int64_t count) {
   if ((rc = ensure_rope(m, cf.max_positions))) return rc;
   FL_CUDA(c, cudaStreamSynchronize(c->stream));
   m->loaded = true;
+  return FLETCHER_OK;
+}
+
+// ---- Cuda_Model_LoadTensor: one checkpoint tensor by its reference name, any dtype, placed
+// straight into the model's device layout (no host fp32 copy of the model).
+
+// Checkpoint tensor names in LoadFromSafeTensors order (weights/loader.go:257-293).
+static const char* kLayerSuffix[16] = {
+    "attention.self.query.weight", "attention.self.query.bias", "attention.self.key.weight",
+    "attention.self.key.bias", "attention.self.value.weight", "attention.self.value.bias",
+    "attention.output.dense.weight", "attention.output.dense.bias", "attention.output.LayerNorm.weight",
+    "attention.output.LayerNorm.bias", "intermediate.dense.weight", "intermediate.dense.bias",
+    "output.dense.weight", "output.dense.bias", "output.LayerNorm.weight", "output.LayerNorm.bias"};
+static const char* kHeadNames[5] = {"embeddings.word_embeddings.weight", "embeddings.position_embeddings.weight",
+                                     "embeddings.token_type_embeddings.weight", "embeddings.LayerNorm.weight",
+                                     "embeddings.LayerNorm.bias"};
+
+int64_t tensor_count(const FletcherBertConfig* c) { return 5 + 16ll * c->num_layers + 2; }
+
+// name -> index in raw order (-1 if unknown).
+static int64_t tensor_index(const FletcherBertConfig* cf, const char* name) {
+  for (int i = 0; i < 5; i++)
+    if (!strcmp(name, kHeadNames[i])) return i;
+  if (!strcmp(name, "pooler.dense.weight")) return 5 + 16ll * cf->num_layers;
+  if (!strcmp(name, "pooler.dense.bias")) return 5 + 16ll * cf->num_layers + 1;
+  int layer = -1, used = 0;
+  if (sscanf(name, "encoder.layer.%d.%n", &layer, &used) == 1 && used > 0 && layer >= 0 && layer < cf->num_layers)
+    for (int j = 0; j < 16; j++)
+      if (!strcmp(name + used, kLayerSuffix[j])) return 5 + 16ll * layer + j;
+  return -1;
+}
+
+// Expected (rows, cols) of tensor `idx` as the raw order stores it ((in,out) for Linear weights;
+// vectors as (1, n)), and whether it is a Linear weight (loader.go:231-234).
+static void tensor_shape(const Model* m, int64_t idx, int64_t* rows, int64_t* cols, bool* linear) {
+  const FletcherBertConfig& cf = m->cfg;
+  const int64_t H = m->H, I = m->I, Iup = m->Iup;
+  *linear = false;
+  if (idx < 5) {
+    const int64_t r[5] = {cf.vocab_size, cf.max_positions, 2, 1, 1};
+    *rows = r[idx];
+    *cols = H;
+    return;
+  }
+  const int64_t L = cf.num_layers;
+  if (idx >= 5 + 16 * L) {
+    *linear = idx == 5 + 16 * L;
+    *rows = *linear ? H : 1;
+    *cols = H;
+    return;
+  }
+  const int j = (int)((idx - 5) % 16);
+  const int64_t shapes[16][2] = {{H, H}, {1, H}, {H, H}, {1, H}, {H, H}, {1, H}, {H, H}, {1, H}, {1, H}, {1, H},
+                                 {H, Iup}, {1, Iup}, {I, H}, {1, H}, {1, H}, {1, H}};
+  *rows = shapes[j][0];
+  *cols = shapes[j][1];
+  *linear = j == 0 || j == 2 || j == 4 || j == 6 || j == 10 || j == 12;
+}
+
+static bool host_all_zero(const void* p, int32_t dt, int64_t n) {
+  const int64_t bytes = n * dtype_size(dt);
+  const uint8_t* b = (const uint8_t*)p;
+  for (int64_t i = 0; i < bytes; i++)  // +0 only; a -0 bias is kept (it is a no-op either way)
+    if (b[i]) return false;
+  return true;
+}
+
+// A vector (bias, LayerNorm parameter) into an fp32 device array, allocated on first use.
+static int32_t place_vec_f32(Model* m, float** d, int64_t total, int64_t off, const void* src_dev, int32_t sdt,
+                             int64_t n) {
+  int32_t rc;
+  if (!*d && (rc = own(m, (void**)d, total * 4))) return rc;
+  return launch_cast(m->c, sdt, src_dev, FLETCHER_F32, *d + off, n);
+}
+
+static int32_t load_tensor(Model* m, const char* name, int32_t sdt, const void* data, int64_t rows, int64_t cols,
+                           int32_t transposed) {
+  Ctx* c = m->c;
+  const FletcherBertConfig& cf = m->cfg;
+  FL_CHECK(c, name && data, "LoadTensor: null argument");
+  FL_CHECK(c, sdt >= 0 && sdt <= 2, "LoadTensor %s: bad dtype %d", name, sdt);
+  const int64_t idx = tensor_index(&cf, name);
+  FL_CHECK(c, idx >= 0, "LoadTensor: tensor %s is not part of this model", name);  // loader.go:187-190
+  int64_t er = 0, ec = 0;
+  bool linear = false;
+  tensor_shape(m, idx, &er, &ec, &linear);
+  FL_CHECK(c, rows * cols == er * ec, "LoadTensor %s: size mismatch: expected %lld, got %lldx%lld", name,
+           (long long)(er * ec), (long long)rows, (long long)cols);  // loader.go:200-202
+  FL_CHECK(c, !transposed || linear, "LoadTensor %s: only Linear weights may be given transposed", name);
+  if (linear)
+    FL_CHECK(c, transposed ? (rows == ec && cols == er) : (rows == er && cols == ec),
+             "LoadTensor %s: shape mismatch: got (%lld, %lld), expected %s (%lld, %lld)", name, (long long)rows,
+             (long long)cols, transposed ? "(out, in)" : "(in, out)", (long long)(transposed ? ec : er),
+             (long long)(transposed ? er : ec));
+  const int64_t n = er * ec;
+  const bool zero = !linear && er == 1 && host_all_zero(data, sdt, n);
+  const int64_t H = m->H, L = cf.num_layers;
+  if ((int64_t)m->layers.size() != L) m->layers.assign(L, Layer());
+  if ((int64_t)m->tensor_loaded.size() != tensor_count(&cf)) m->tensor_loaded.assign(tensor_count(&cf), 0);
+  clear_graphs(m);  // captured graphs may hold a pointer this load allocates
+  m->loaded = false;
+
+  // Stage the host tensor on the device as it is (sdt, given layout).
+  void* stage = nullptr;
+  int32_t rc = dev_alloc(c, &stage, n * dtype_size(sdt));
+  if (rc) return rc;
+  struct StageFree {
+    Ctx* c;
+    void* p;
+    int64_t b;
+    ~StageFree() { dev_free(c, p, b); }
+  } sf{c, stage, n * dtype_size(sdt)};
+  FL_CUDA(c, cudaMemcpyAsync(stage, data, n * dtype_size(sdt), cudaMemcpyHostToDevice, c->stream));
+
+  const bool sixteen = m->dtype != FLETCHER_F32;
+  const bool hf = sdt == FLETCHER_F32 && c->half_mode == FLETCHER_HALF_REFERENCE;
+  auto table = [&](void** d, int64_t elems) -> int32_t {  // model-dtype table, first `elems` values
+    int32_t r;
+    if (!*d && (r = own(m, d, elems * dtype_size(m->dtype)))) return r;
+    return launch_cast(c, sdt, stage, m->dtype, *d, elems, hf);
+  };
+  // Linear weight of (in,out) [K, N] into `d` (allocated [Ntot, K] K-major for 16-bit models,
+  // or (in,out) [K, Ntot] for fp32) at output offset `off`.
+  auto weight = [&](void** d, int64_t K, int64_t N, int64_t Ntot, int64_t off, int perm, int bn) -> int32_t {
+    int32_t r;
+    if (!*d && (r = own(m, d, K * Ntot * dtype_size(m->dtype)))) return r;
+    return launch_place_weight(c, sdt, stage, K, N, transposed, m->dtype, *d, sixteen ? 1 : 0, Ntot, off, perm, bn);
+  };
+  auto bias = [&](float** d, int64_t total, int64_t off, int64_t len) -> int32_t {
+    if (zero) {  // an all-zero bias adds nothing; keep it absent (or clear a loaded one)
+      if (*d) FL_CUDA(c, cudaMemsetAsync(*d + off, 0, len * 4, c->stream));
+      return FLETCHER_OK;
+    }
+    return place_vec_f32(m, d, total, off, stage, sdt, len);
+  };
+
+  if (idx == 0) {
+    rc = table(&m->word, (int64_t)cf.vocab_size * H);
+  } else if (idx == 1) {
+    rc = cf.position_type == 0 ? table(&m->ptab, (int64_t)cf.max_positions * H) : FLETCHER_OK;  // RoPE: unused
+  } else if (idx == 2) {
+    rc = table(&m->type0, H);  // token type 0 only (bert.go:242-245)
+  } else if (idx == 3 || idx == 4) {
+    rc = place_vec_f32(m, idx == 3 ? &m->eln_g : &m->eln_b, H, 0, stage, sdt, H);
+  } else if (idx >= 5 + 16 * L) {
+    if (idx == 5 + 16 * L) {  // the pooler stays fp32 (in,out) in every mode (bert.go:459-477)
+      if (!m->wp && (rc = own(m, (void**)&m->wp, H * H * 4))) return rc;
+      rc = launch_place_weight(c, sdt, stage, H, H, transposed, FLETCHER_F32, m->wp, 0, H, 0, 0, 0);
+    } else {
+      rc = place_vec_f32(m, &m->bp, H, 0, stage, sdt, H);
+    }
+  } else {
+    Layer& Ly = m->layers[(idx - 5) / 16];
+    const int j = (int)((idx - 5) % 16);
+    const bool swiglu = cf.activation == FLETCHER_ACT_SWIGLU;
+    const int perm = swiglu && sixteen ? 1 : 0;
+    switch (j) {
+      case 0: case 2: case 4: rc = weight(&Ly.wqkv, H, H, 3 * H, (j / 2) * H, 0, 0); break;
+      case 1: case 3: case 5: rc = bias(&Ly.bqkv, 3 * H, (j / 2) * H, H); break;
+      case 6: rc = weight(&Ly.wo, H, H, H, 0, 0, 0); break;
+      case 7: rc = bias(&Ly.bo, H, 0, H); break;
+      case 8: rc = place_vec_f32(m, &Ly.ln1g, H, 0, stage, sdt, H); break;
+      case 9: rc = place_vec_f32(m, &Ly.ln1b, H, 0, stage, sdt, H); break;
+      case 10: rc = weight(&Ly.wi, H, m->Iup, m->Iup, 0, perm, m->bn_up); break;
+      case 11:
+        if (perm && !zero) {  // interleave like the weight rows: place the [1, Iup] row as K = 1
+          if (!Ly.bi && (rc = own(m, (void**)&Ly.bi, m->Iup * 4))) return rc;
+          rc = launch_place_weight(c, sdt, stage, 1, m->Iup, 0, FLETCHER_F32, Ly.bi, 1, 0, 0, perm, m->bn_up);
+        } else {
+          rc = bias(&Ly.bi, m->Iup, 0, m->Iup);
+        }
+        break;
+      case 12: rc = weight(&Ly.wd, m->I, H, H, 0, 0, 0); break;
+      case 13: rc = bias(&Ly.bd, H, 0, H); break;
+      case 14: rc = place_vec_f32(m, &Ly.ln2g, H, 0, stage, sdt, H); break;
+      default: rc = place_vec_f32(m, &Ly.ln2b, H, 0, stage, sdt, H); break;
+    }
+  }
+  if (rc) return rc;
+  FL_CUDA(c, cudaStreamSynchronize(c->stream));  // the caller may free `data` on return
+  m->tensor_loaded[idx] = 1;
+  bool all = true;
+  for (uint8_t v : m->tensor_loaded) all = all && v;
+  if (all) {
+    if ((rc = ensure_rope(m, cf.max_positions))) return rc;
+    m->loaded = true;
+  }
   return FLETCHER_OK;
 }
 
@@ -644,6 +847,31 @@ int32_t Cuda_Model_LoadRaw(CudaModelRef model, const float* blob, int64_t count)
   return load_raw(m, blob, count);
 }
 
+int32_t Cuda_Model_LoadTensor(CudaModelRef model, const char* name, int32_t dtype, const void* data, int64_t rows,
+                              int64_t cols, int32_t transposed) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(m->c);
+  return load_tensor(m, name, dtype, data, rows, cols, transposed);
+}
+
+int32_t Cuda_Model_TensorCount(const FletcherBertConfig* cfg) { return cfg ? (int32_t)tensor_count(cfg) : -1; }
+
+int32_t Cuda_Model_TensorName(const FletcherBertConfig* cfg, int32_t index, char* buf, int32_t len) {
+  if (!cfg || !buf || len <= 0 || index < 0 || index >= tensor_count(cfg)) return FLETCHER_ERR_INVALID;
+  const int64_t L = cfg->num_layers;
+  if (index < 5) snprintf(buf, len, "%s", kHeadNames[index]);
+  else if (index == 5 + 16 * L) snprintf(buf, len, "pooler.dense.weight");
+  else if (index == 5 + 16 * L + 1) snprintf(buf, len, "pooler.dense.bias");
+  else snprintf(buf, len, "encoder.layer.%d.%s", (int)((index - 5) / 16), kLayerSuffix[(index - 5) % 16]);
+  return FLETCHER_OK;
+}
+
+int32_t Cuda_Model_IsLoaded(CudaModelRef model) {
+  Model* m = reinterpret_cast<Model*>(model);
+  return m && m->loaded ? 1 : 0;
+}
+
 int32_t Cuda_Model_ForwardBatchDevice(CudaModelRef model, const int32_t* d_ids, const int32_t* lengths, int32_t B,
                                       int32_t pooling, float* d_out) {
   Model* m = reinterpret_cast<Model*>(model);
@@ -677,8 +905,9 @@ int32_t Cuda_Model_ForwardBatchEx(CudaModelRef model, const int32_t* ids, const 
   const int64_t n = (int64_t)B * m->H;
   if (out_dtype == FLETCHER_F32) {
     FL_CUDA(c, cudaMemcpyAsync(out, m->d_out, n * 4, cudaMemcpyDeviceToHost, c->stream));
-  } else {  // cast on the device (round to nearest even), copy half the bytes
-    if ((rc = launch_cast(c, FLETCHER_F32, m->d_out, out_dtype, m->d_cls, n))) return rc;
+  } else {  // cast on the device (fp16 with the context's conversion, bf16 RNE), copy half the bytes
+    if ((rc = launch_cast(c, FLETCHER_F32, m->d_out, out_dtype, m->d_cls, n, c->half_mode == FLETCHER_HALF_REFERENCE)))
+      return rc;
     FL_CUDA(c, cudaMemcpyAsync(out, m->d_cls, n * 2, cudaMemcpyDeviceToHost, c->stream));
   }
   FL_CUDA(c, cudaStreamSynchronize(c->stream));
@@ -725,7 +954,8 @@ int32_t Cuda_Model_ForwardBatchAsync(CudaModelRef model, const int32_t* ids, con
   if (out_dtype == FLETCHER_F32) {
     FL_CUDA(c, cudaMemcpyAsync(out, m->d_out, n * 4, cudaMemcpyDeviceToHost, c->stream));
   } else {
-    if ((rc = launch_cast(c, FLETCHER_F32, m->d_out, out_dtype, m->d_cls, n))) return rc;
+    if ((rc = launch_cast(c, FLETCHER_F32, m->d_out, out_dtype, m->d_cls, n, c->half_mode == FLETCHER_HALF_REFERENCE)))
+      return rc;
     FL_CUDA(c, cudaMemcpyAsync(out, m->d_cls, n * 2, cudaMemcpyDeviceToHost, c->stream));
   }
   const int slot = (int)(m->async_issued % Model::kAsyncSlots);

@@ -92,6 +92,13 @@ extern "C" int32_t Cuda_Attention_VarLen_NoAlloc(CudaContextRef ctx, CudaBufferR
            "AttentionVarLen_NoAlloc: batch needs %lld scratch ints, the limit is %d (FLETCHER_NOALLOC_SCRATCH_INTS)",
            (long long)need, (int)FLETCHER_NOALLOC_SCRATCH_INTS);
   if (T == 0) return FLETCHER_OK;
+  // The metadata goes through a pageable host array, which a stream capture cannot record (and a
+  // recorded copy would replay whatever a later call left in it): refuse capture outright.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  FL_CUDA(c, cudaStreamIsCapturing(c->stream, &cap));
+  FL_CHECK(c, cap == cudaStreamCaptureStatusNone,
+           "AttentionVarLen_NoAlloc: cannot be captured into a CUDA graph (its metadata is copied from a host array)");
+  touch(o);
 
   std::lock_guard<std::mutex> lock(g_mu);
   int32_t* dscr = nullptr;

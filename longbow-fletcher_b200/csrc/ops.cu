@@ -526,23 +526,26 @@ int32_t launch_has_nan(Ctx* c, int32_t dt, const void* x, int64_t n, int32_t* fl
   return FLETCHER_OK;
 }
 
+// ref: fp16 on either side uses the reference's conversion (utils.go:13-91) instead of IEEE
+// round-to-nearest-even; the ABI's Cast and the model's fp16 output transport pass the
+// context's mode, internal casts pass false.
 template <typename S, typename D>
-__global__ void k_cast(const S* s, D* d, int64_t n) {
+__global__ void k_cast(const S* s, D* d, int64_t n, bool ref) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    d[i] = from_f<D>(to_f<S>(s[i]));
+    d[i] = from_f_host<D>(to_f_host<S>(s[i], ref), ref);
 }
 template <typename S>
-static void cast_to(Ctx* c, const S* s, int32_t ddt, void* d, int64_t n, int g) {
-  if (ddt == FLETCHER_F32) k_cast<S, float><<<g, 256, 0, c->stream>>>(s, (float*)d, n);
-  else if (ddt == FLETCHER_BF16) k_cast<S, __nv_bfloat16><<<g, 256, 0, c->stream>>>(s, (__nv_bfloat16*)d, n);
-  else k_cast<S, __half><<<g, 256, 0, c->stream>>>(s, (__half*)d, n);
+static void cast_to(Ctx* c, const S* s, int32_t ddt, void* d, int64_t n, int g, bool ref) {
+  if (ddt == FLETCHER_F32) k_cast<S, float><<<g, 256, 0, c->stream>>>(s, (float*)d, n, ref);
+  else if (ddt == FLETCHER_BF16) k_cast<S, __nv_bfloat16><<<g, 256, 0, c->stream>>>(s, (__nv_bfloat16*)d, n, ref);
+  else k_cast<S, __half><<<g, 256, 0, c->stream>>>(s, (__half*)d, n, ref);
 }
-int32_t launch_cast(Ctx* c, int32_t sdt, const void* s, int32_t ddt, void* d, int64_t n) {
+int32_t launch_cast(Ctx* c, int32_t sdt, const void* s, int32_t ddt, void* d, int64_t n, bool ref) {
   if (n <= 0) return FLETCHER_OK;
   const int g = grid_for(n, 256);
-  if (sdt == FLETCHER_F32) cast_to<float>(c, (const float*)s, ddt, d, n, g);
-  else if (sdt == FLETCHER_BF16) cast_to<__nv_bfloat16>(c, (const __nv_bfloat16*)s, ddt, d, n, g);
-  else cast_to<__half>(c, (const __half*)s, ddt, d, n, g);
+  if (sdt == FLETCHER_F32) cast_to<float>(c, (const float*)s, ddt, d, n, g, ref);
+  else if (sdt == FLETCHER_BF16) cast_to<__nv_bfloat16>(c, (const __nv_bfloat16*)s, ddt, d, n, g, ref);
+  else cast_to<__half>(c, (const __half*)s, ddt, d, n, g, ref);
   FL_LAUNCH(c);
   return FLETCHER_OK;
 }
@@ -560,7 +563,7 @@ __device__ __forceinline__ int64_t packed_src_col(int64_t n, int64_t N, int perm
 
 template <typename S, typename T>
 __global__ void k_pack_kmajor(const S* __restrict__ src, int64_t K, int64_t N, T* __restrict__ dst, int perm,
-                              int block_n) {
+                              int block_n, bool ref = false) {
   __shared__ float tile[32][33];
   const int64_t k0 = (int64_t)blockIdx.x * 32, n0 = (int64_t)blockIdx.y * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -570,7 +573,7 @@ __global__ void k_pack_kmajor(const S* __restrict__ src, int64_t K, int64_t N, T
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int64_t n = n0 + i, k = k0 + threadIdx.x;
-    if (n < N && k < K) dst[n * K + k] = from_f<T>(tile[threadIdx.x][i]);
+    if (n < N && k < K) dst[n * K + k] = from_f_host<T>(tile[threadIdx.x][i], ref);
   }
 }
 
@@ -578,8 +581,78 @@ int32_t launch_pack_weight_kmajor(Ctx* c, const float* src, int64_t K, int64_t N
                                   int32_t perm, int32_t block_n) {
   dim3 grid((unsigned)((K + 31) / 32), (unsigned)((N + 31) / 32)), blk(32, 8);
   if (dt == FLETCHER_BF16) k_pack_kmajor<float, __nv_bfloat16><<<grid, blk, 0, c->stream>>>(src, K, N, (__nv_bfloat16*)dst, perm, block_n);
-  else if (dt == FLETCHER_F16) k_pack_kmajor<float, __half><<<grid, blk, 0, c->stream>>>(src, K, N, (__half*)dst, perm, block_n);
+  else if (dt == FLETCHER_F16)  // fp32 host weights -> fp16 as the reference's CopyFromFloat32 converts them
+    k_pack_kmajor<float, __half><<<grid, blk, 0, c->stream>>>(src, K, N, (__half*)dst, perm, block_n,
+                                                              c->half_mode == FLETCHER_HALF_REFERENCE);
   else k_pack_kmajor<float, float><<<grid, blk, 0, c->stream>>>(src, K, N, (float*)dst, perm, block_n);
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+// Places one (in,out) [K, N] Linear weight, given as stored in a checkpoint (src_t: (out,in)
+// [N, K], the SafeTensors / PyTorch layout) in any dtype, into a model weight buffer of another
+// dtype: K-major rows [row_off + n', K] with the SwiGLU interleave applied to n (dst_kmajor),
+// or (in,out) columns [K, ld] at col_off (fp32 models).  A 32x32 tile is transposed through
+// shared memory when the source and destination layouts disagree, so both sides stay coalesced.
+__device__ __forceinline__ int64_t packed_dst_row(int64_t n, int64_t N, int perm, int block_n) {
+  if (perm == 0) return n;
+  const int64_t half = block_n / 2, I = N / 2;
+  const int64_t u = n < I ? n : n - I;
+  return (u / half) * block_n + (n < I ? 0 : half) + u % half;
+}
+
+template <typename S, typename D>
+__global__ void k_place_weight(const S* __restrict__ src, int64_t K, int64_t N, int src_t, D* __restrict__ dst,
+                               int dst_kmajor, int64_t ld, int64_t off, int perm, int block_n, bool ref) {
+  __shared__ float tile[32][33];
+  const int64_t k0 = (int64_t)blockIdx.x * 32, n0 = (int64_t)blockIdx.y * 32;
+  // Load: lanes run along the source's contiguous index.
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t k = src_t ? k0 + threadIdx.x : k0 + i, n = src_t ? n0 + i : n0 + threadIdx.x;
+    float v = 0.f;
+    if (k < K && n < N) v = to_f<S>(src_t ? src[n * K + k] : src[k * N + n]);
+    if (src_t) tile[i][threadIdx.x] = v;  // tile[n][k]
+    else tile[threadIdx.x][i] = v;        // tile[n][k]
+  }
+  __syncthreads();
+  // Store: lanes run along the destination's contiguous index.
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    if (dst_kmajor) {
+      const int64_t n = n0 + i, k = k0 + threadIdx.x;
+      if (n < N && k < K) dst[(off + packed_dst_row(n, N, perm, block_n)) * K + k] = from_f_host<D>(tile[i][threadIdx.x], ref);
+    } else {
+      const int64_t k = k0 + i, n = n0 + threadIdx.x;
+      if (n < N && k < K) dst[k * ld + off + n] = from_f_host<D>(tile[threadIdx.x][i], ref);
+    }
+  }
+}
+
+template <typename S>
+static void place_from(Ctx* c, dim3 g, dim3 b, const S* src, int64_t K, int64_t N, int src_t, int32_t ddt, void* dst,
+                       int dst_kmajor, int64_t ld, int64_t off, int perm, int block_n, bool ref) {
+  if (ddt == FLETCHER_F32)
+    k_place_weight<S, float><<<g, b, 0, c->stream>>>(src, K, N, src_t, (float*)dst, dst_kmajor, ld, off, perm, block_n, ref);
+  else if (ddt == FLETCHER_BF16)
+    k_place_weight<S, __nv_bfloat16><<<g, b, 0, c->stream>>>(src, K, N, src_t, (__nv_bfloat16*)dst, dst_kmajor, ld, off,
+                                                             perm, block_n, ref);
+  else
+    k_place_weight<S, __half><<<g, b, 0, c->stream>>>(src, K, N, src_t, (__half*)dst, dst_kmajor, ld, off, perm, block_n,
+                                                      ref);
+}
+
+int32_t launch_place_weight(Ctx* c, int32_t sdt, const void* src, int64_t K, int64_t N, int src_t, int32_t ddt,
+                            void* dst, int dst_kmajor, int64_t ld, int64_t off, int perm, int block_n) {
+  if (K <= 0 || N <= 0) return FLETCHER_OK;
+  // fp32 checkpoint values become fp16 as the reference's CopyFromFloat32 converts them.
+  const bool ref = sdt == FLETCHER_F32 && c->half_mode == FLETCHER_HALF_REFERENCE;
+  dim3 grid((unsigned)((K + 31) / 32), (unsigned)((N + 31) / 32)), blk(32, 8);
+  if (sdt == FLETCHER_F32)
+    place_from<float>(c, grid, blk, (const float*)src, K, N, src_t, ddt, dst, dst_kmajor, ld, off, perm, block_n, ref);
+  else if (sdt == FLETCHER_BF16)
+    place_from<__nv_bfloat16>(c, grid, blk, (const __nv_bfloat16*)src, K, N, src_t, ddt, dst, dst_kmajor, ld, off, perm,
+                              block_n, ref);
+  else
+    place_from<__half>(c, grid, blk, (const __half*)src, K, N, src_t, ddt, dst, dst_kmajor, ld, off, perm, block_n, ref);
   FL_LAUNCH(c);
   return FLETCHER_OK;
 }

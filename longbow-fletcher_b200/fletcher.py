@@ -25,6 +25,7 @@ LIB_PATH = os.path.join(HERE, "libcuda_fletcher.so")
 F32, F16, BF16 = 0, 1, 2
 ACT_IDENTITY, ACT_GELU, ACT_TANH, ACT_SOFTMAX, ACT_SWIGLU = 0, 1, 2, 3, 4
 POOL_CLS_TANH, POOL_MEAN_L2 = 0, 1
+HALF_REFERENCE, HALF_RNE = 0, 1
 DTYPES = {"f32": F32, "f16": F16, "bf16": BF16}
 _NP = {F32: np.float32, F16: np.float16}
 
@@ -94,6 +95,16 @@ def _sig(L):
         "Cuda_GetLaunchCount": (i64, [vp]),
         "Cuda_Debug_WaitTimeoutProbe": (i32, [vp, i64, i32]),
         "Cuda_Model_Free": (i32, [vp]),
+        "Cuda_SetHalfConversion": (i32, [vp, i32]),
+        "Cuda_Model_LoadTensor": (i32, [vp, ctypes.c_char_p, i32, vp, i64, i64, i32]),
+        "Cuda_Model_TensorCount": (i32, [vp]),
+        "Cuda_Model_TensorName": (i32, [vp, i32, ctypes.c_char_p, i32]),
+        "Cuda_Model_IsLoaded": (i32, [vp]),
+        "Cuda_At": (i32, [vp, i64, i64, f32p]),
+        "Cuda_Set": (i32, [vp, i64, i64, f32]),
+        "Cuda_Copy": (i32, [vp, vp, i64, vp, i64, i64]),
+        "Cuda_Slice": (i32, [vp, vp, i64, i64, i64, i64, vp]),
+        "Cuda_Mul": (i32, [vp, vp, i32, vp, i32, vp, i64, i64, i64]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -175,6 +186,10 @@ class Backend:
     def device_count(self):
         return lib().Cuda_GetDeviceCount()
 
+    def set_half_conversion(self, mode):
+        """FLETCHER_HALF_REFERENCE (the reference's utils.go bytes, default) or FLETCHER_HALF_RNE."""
+        self.check(lib().Cuda_SetHalfConversion(self.ctx, mode))
+
     def vram_usage(self):
         a, t = ctypes.c_int64(), ctypes.c_int64()
         self.check(lib().Cuda_MemGetInfo(self.ctx, ctypes.byref(a), ctypes.byref(t)))
@@ -193,10 +208,14 @@ class Backend:
 
 
 class Tensor:
-    """device.Tensor: a dtype-tagged device buffer of (rows, cols)."""
+    """device.Tensor: a dtype-tagged device buffer of (rows, cols).  T() returns a transposed
+    view sharing the buffer (cpu_backend.go:306-314); only Mul reads the flag, as in the
+    reference, where every other op sees the stored layout."""
 
     def __init__(self, be: Backend, r, c, dtype, data=None):
         self.be, self.rows, self.cols, self.dtype = be, int(r), int(c), dtype
+        self.trans = False
+        self._owner = None
         self.buf = lib().Cuda_AllocTensor(be.ctx, self.rows, self.cols, dtype)
         if not self.buf:
             be.check(3)
@@ -205,13 +224,52 @@ class Tensor:
 
     def __del__(self):
         try:
-            if self.buf and self.be.ctx:
+            if self._owner is None and self.buf and self.be.ctx:
                 lib().Cuda_FreeBuffer(self.be.ctx, self.buf)
         except Exception:
             pass
 
     def dims(self):
-        return self.rows, self.cols
+        return (self.cols, self.rows) if self.trans else (self.rows, self.cols)
+
+    def T(self):
+        v = Tensor.__new__(Tensor)
+        v.be, v.rows, v.cols, v.dtype, v.buf = self.be, self.rows, self.cols, self.dtype, self.buf
+        v.trans = not self.trans
+        v._owner = self._owner or self  # keeps the buffer alive; the view never frees it
+        return v
+
+    def at(self, i, j):
+        r = ctypes.c_float()
+        self.be.check(lib().Cuda_At(self.buf, i, j, ctypes.byref(r)))
+        return r.value
+
+    def set(self, i, j, v):
+        self.be.check(lib().Cuda_Set(self.buf, i, j, float(v)))
+
+    def copy(self, other: "Tensor"):
+        """device.Tensor.Copy: same dims, element-wise (cpu_backend.go:259-286)."""
+        if self.dims() != other.dims():
+            raise FletcherError(1, f"Copy: dimension mismatch {self.dims()} <- {other.dims()}")
+        self.be.check(lib().Cuda_Copy(self.be.ctx, self.buf, 0, other.buf, 0, self.rows * self.cols))
+
+    def slice(self, i, k, j, l):
+        """device.Tensor.Slice: a new tensor holding a copy of [i:k, j:l] (cpu_backend.go:288-303)."""
+        if k - i <= 0 or l - j <= 0:
+            raise FletcherError(1, "Slice: invalid dimensions")
+        out = Tensor(self.be, k - i, l - j, self.dtype)
+        self.be.check(lib().Cuda_Slice(self.be.ctx, self.buf, i, k, j, l, out.buf))
+        return out
+
+    def mul(self, a: "Tensor", b: "Tensor"):
+        """device.Tensor.Mul: self = a . b, honouring T() views (cpu_backend.go:316-372)."""
+        ar, ac = a.dims()
+        br, bc = b.dims()
+        if ac != br:
+            raise FletcherError(1, f"Mul: dimension mismatch a_cols={ac} b_rows={br}")
+        if self.dims() != (ar, bc):
+            raise FletcherError(1, f"Mul: result tensor dimension mismatch. Expected {ar}x{bc}, got {self.dims()}")
+        self.be.check(lib().Cuda_Mul(self.be.ctx, a.buf, int(a.trans), b.buf, int(b.trans), self.buf, ar, bc, ac))
 
     def ptr(self):
         return lib().Cuda_GetBufferContents(self.buf)
@@ -326,6 +384,17 @@ class BertModel:
     def load_raw(self, blob):
         b = np.ascontiguousarray(blob, np.float32)
         self.be.check(lib().Cuda_Model_LoadRaw(self.h, _f32p(b), b.size))
+
+    def load_tensor(self, name, array, dtype, transposed=False):
+        """One checkpoint tensor by its reference name; `array` holds the raw values of `dtype`
+        (float32, float16, or bfloat16 bit patterns as uint16), 1-D or 2-D."""
+        a = np.ascontiguousarray(array)
+        rows, cols = (1, a.size) if a.ndim <= 1 else (a.shape[0], int(np.prod(a.shape[1:])))
+        self.be.check(lib().Cuda_Model_LoadTensor(self.h, name.encode(), dtype, a.ctypes.data, rows, cols,
+                                                  int(transposed)))
+
+    def is_loaded(self):
+        return bool(lib().Cuda_Model_IsLoaded(self.h))
 
     def forward_batch(self, ids, lengths, pooling=POOL_MEAN_L2):
         ids = np.ascontiguousarray(ids, np.int32)

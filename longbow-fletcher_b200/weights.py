@@ -100,6 +100,48 @@ def _is_linear_weight(name: str, arr: np.ndarray) -> bool:
     return name.endswith(".weight") and arr.ndim == 2 and "embeddings" not in name and "LayerNorm" not in name
 
 
+def read_safetensors_raw(path: str) -> dict:
+    """name -> (raw ndarray in the stored dtype: float32, float16, or uint16 bfloat16 bits; dtype tag)."""
+    with open(path, "rb") as f:
+        (n,) = struct.unpack("<Q", f.read(8))
+        if n > 100 * 1024 * 1024:  # loader.go:171-173
+            raise ValueError(f"header size too large: {n}")
+        header = json.loads(f.read(n))
+        body = f.read()
+    out = {}
+    for name, info in header.items():
+        if name == "__metadata__":
+            continue
+        dt = info["dtype"]
+        if dt not in _DTYPES:
+            raise ValueError(f"tensor {name!r}: dtype {dt} not supported (F32, F16, BF16)")
+        npdt, size = _DTYPES[dt]
+        a, b = info["data_offsets"]
+        count = int(np.prod(info["shape"])) if info["shape"] else 1
+        if b - a != count * size:
+            raise ValueError(f"tensor {name!r} byte size mismatch: {b - a} != {count * size}")
+        out[name] = (np.frombuffer(body[a:b], dtype=npdt).reshape(info["shape"]), dt)
+    return out
+
+
+def load_safetensors_direct(model, path: str) -> None:
+    """Loads a SafeTensors checkpoint (F32, F16 or BF16) into a device model tensor by tensor
+    through Cuda_Model_LoadTensor: the stored bytes go to the device as they are and are
+    converted and packed there, so no fp32 copy of the model is built on the host.  The
+    reference's names and transpose rule (loader.go:229-251) decide which tensors arrive
+    (out, in)."""
+    import fletcher
+    codes = {"F32": fletcher.F32, "F16": fletcher.F16, "BF16": fletcher.BF16}
+    tensors = read_safetensors_raw(path)
+    for hf, _ in hf_names(model.cfg):
+        if hf not in tensors:
+            raise KeyError(f"tensor {hf!r} not found in SafeTensors file")  # loader.go:187-190
+        arr, dt = tensors[hf]
+        model.load_tensor(hf, arr, codes[dt], transposed=_is_linear_weight(hf, arr))
+    if not model.is_loaded():
+        raise RuntimeError("checkpoint did not cover every model tensor")
+
+
 def blob_from_safetensors(path: str, cfg: synth.BertConfig) -> np.ndarray:
     """The raw float32 blob (LoadFromRawBinary order) from a SafeTensors checkpoint."""
     tensors = read_safetensors(path)

@@ -55,6 +55,10 @@ def lib(threads: int | None = None):
                                 ctypes.c_int64, ctypes.c_float, f32p, ctypes.c_int64, f32p,
                                 ctypes.c_int64, f32p, ctypes.c_int64]
         L.ref_rope.argtypes = [f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, i32p, ctypes.c_double]
+        L.ref_linear_activation.argtypes = [f32p, ctypes.c_int64, ctypes.c_int64, f32p, ctypes.c_int64, f32p,
+                                            ctypes.c_int, f32p]
+        L.ref_attention.argtypes = [f32p, f32p, f32p, f32p, ctypes.c_int64, ctypes.c_int, i32p, ctypes.c_int,
+                                    ctypes.c_float]
         L.ref_forward.argtypes = [ctypes.c_void_p, f32p, ctypes.c_int64, i32p, i32p, ctypes.c_int32,
                                   ctypes.c_int32, f32p, f32p, f32p]
         _lib = L

@@ -264,6 +264,38 @@ void ref_sgemm(int ta, int tb, int64_t m, int64_t n, int64_t k, float alpha, con
                int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc) {
   sgemm(ta != 0, tb != 0, m, n, k, alpha, a, lda, b, ldb, c, ldc);
 }
+// LinearActivation (cpu_backend.go:626-660): y = act(x . w + b); for SwiGLU (act 4) y has n/2
+// columns, silu(first half) * second half with float64 exp; GELU (1) / Tanh (2) the fast forms.
+void ref_linear_activation(const float* x, int64_t rows, int64_t k, const float* w, int64_t n, const float* b,
+                           int act, float* y) {
+  std::vector<float> full((size_t)(rows * n));
+  linear(x, rows, k, w, n, b, full.data());
+  if (act == 4) {
+    const int64_t I = n / 2;
+    for (int64_t r = 0; r < rows; r++)
+      for (int64_t i = 0; i < I; i++) {
+        float xx = full[r * n + i], yy = full[r * n + i + I];
+        float sw = xx / (1.0f + (float)std::exp((double)(-xx)));
+        y[r * I + i] = sw * yy;
+      }
+    return;
+  }
+  for (int64_t i = 0; i < rows * n; i++)
+    y[i] = act == 1 ? gelu_fast(full[i]) : act == 2 ? tanh_fast(full[i]) : full[i];
+}
+
+// CPUTensor.Attention over packed sequences of the given lengths (cpu_backend.go:662-758).
+void ref_attention(const float* q, const float* k, const float* v, float* out, int64_t c, int nh,
+                   const int32_t* lens, int B, float scale) {
+  std::vector<int64_t> starts(B);
+  int64_t t = 0;
+  for (int i = 0; i < B; i++) {
+    starts[i] = t;
+    t += lens[i];
+  }
+  attention(q, k, v, out, c, nh, starts.data(), lens, B, scale);
+}
+
 void ref_rope(float* t, int64_t rows, int nh, int dh, const int32_t* pos, double base) {
   apply_rope(t, rows, nh, dh, pos, base);
 }

@@ -88,3 +88,59 @@ def bf16_round(x):
     u = x.view(np.uint32).astype(np.uint64)
     u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
     return u.astype(np.uint32).view(np.float32)
+
+
+def f32_to_f16_ref(x):
+    """Float32ToFloat16 (internal/device/utils.go:13-72) vectorised: uint16 bit patterns.
+    NaN -> 0x7E00; +-Inf -> 0x7C00/0xFC00; clamp to +-65504; 0 < |x| < 2^-14 -> signed zero;
+    else sign | (exp-127+15) << 10 | mantissa >> 13 (truncated), 0x7BFF on exponent overflow,
+    signed zero on underflow."""
+    x = np.ascontiguousarray(x, np.float32).copy()
+    nan, pinf, ninf = np.isnan(x), np.isposinf(x), np.isneginf(x)
+    fin = ~(nan | pinf | ninf)
+    x[fin] = np.clip(x[fin], np.float32(-65504.0), np.float32(65504.0))
+    a = np.abs(x)
+    tiny = fin & (a < np.float32(6.103515625e-05)) & (a > 0)
+    bits = x.view(np.uint32)
+    sign = ((bits >> 16) & 0x8000).astype(np.uint32)
+    e = ((bits >> 23) & 0xFF).astype(np.int64) - 127 + 15
+    frac = ((bits >> 13) & 0x3FF).astype(np.uint32)
+    out = (sign | (np.clip(e, 0, 31).astype(np.uint32) << 10) | frac).astype(np.uint32)
+    out = np.where(e >= 0x1F, sign | 0x7BFF, out)
+    out = np.where(e <= 0, sign, out)
+    out = np.where(tiny, np.where(x < 0, 0x8000, 0), out)
+    out = np.where(nan, 0x7E00, out)
+    out = np.where(pinf, 0x7C00, out)
+    out = np.where(ninf, 0xFC00, out)
+    return out.astype(np.uint16)
+
+
+def f16_to_f32_ref(h):
+    """Float16ToFloat32 (internal/device/utils.go:75-91): zero and subnormals -> +0.0; exponent
+    31 keeps the payload (Inf/NaN); normals widen exactly."""
+    h = np.ascontiguousarray(h, np.uint16).astype(np.uint32)
+    sign, e, frac = (h >> 15) & 1, (h >> 10) & 0x1F, h & 0x3FF
+    normal = (sign << 31) | ((e + (127 - 15)) << 23) | (frac << 13)
+    special = (sign << 31) | (0xFF << 23) | (frac << 13)
+    bits = np.where(e == 31, special, normal)
+    bits = np.where(e == 0, 0, bits).astype(np.uint32)
+    return bits.view(np.float32)
+
+
+def half_conversion_probe(n=1_000_000, seed=7):
+    """Inputs for the fp16 byte tests: random floats over the whole fp16 range and beyond, plus
+    NaN, +-Inf, +-65504, +-65520, +-1e6, the subnormal band, +-0 and values whose truncation
+    and round-to-nearest-even differ."""
+    rng = np.random.default_rng(seed)
+    mags = np.exp2(rng.uniform(-30, 20, n)).astype(np.float32)
+    x = (mags * rng.choice(np.array([-1, 1], np.float32), n)).astype(np.float32)
+    special = np.array([np.nan, np.inf, -np.inf, 65504, -65504, 65520, -65520, 65519.99, 1e6, -1e6, 0.0, -0.0,
+                        6.1e-5, -6.1e-5, 6.103515625e-05, -6.103515625e-05, 6.1035156e-05, 5.96e-8, 1e-7, -3e-6,
+                        1.0, -2.0, 1.0009765625, 1.00048828125, 1.0014648, 2049.0, 0.1, -0.3333333], np.float32)
+    return np.concatenate([special, x]).astype(np.float32)
+
+
+def f16_round_ref(x):
+    """float32 -> the value an fp16 tensor holds after CopyFromFloat32 under the reference's
+    conversion (truncation, flush, saturation), as float32."""
+    return f16_to_f32_ref(f32_to_f16_ref(x))

@@ -151,17 +151,24 @@ def test_graph_replay_matches_eager(be, dtype):
 
 @pytest.mark.parametrize("out", ["f16", "bf16"])
 def test_16bit_output_transport(be, out):
-    """ForwardBatchEx returns the vectors rounded to 16 bits on the device: bit-identical to
-    rounding the float32 result on the host."""
+    """ForwardBatchEx returns the vectors converted to 16 bits on the device: fp16 bit-identical
+    to the reference's Float32ToFloat16 (utils.go:13-72) of the float32 result (or to IEEE
+    rounding under FLETCHER_HALF_RNE), bf16 to round-to-nearest-even."""
     import fletcher
-    from helpers import bf16_round
+    from helpers import bf16_round, f32_to_f16_ref
     cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
     m = model(be, cfg, "bf16", 1)
     lens = np.array([50, 3, 129], np.int32)
     ids = synth.make_ids(lens, cfg.vocab_size, 41)
     f32 = m.forward_batch(ids, lens, 1)
     if out == "f16":
-        assert np.array_equal(m.forward_batch_16(ids, lens, 1, fletcher.F16), f32.astype(np.float16))
+        got = m.forward_batch_16(ids, lens, 1, fletcher.F16)
+        assert np.array_equal(got.view(np.uint16), f32_to_f16_ref(f32))
+        be.set_half_conversion(fletcher.HALF_RNE)
+        try:
+            assert np.array_equal(m.forward_batch_16(ids, lens, 1, fletcher.F16), f32.astype(np.float16))
+        finally:
+            be.set_half_conversion(fletcher.HALF_REFERENCE)
     else:
         got = m.forward_batch_16(ids, lens, 1, fletcher.BF16)
         assert np.array_equal((got.astype(np.uint32) << 16).view(np.float32), bf16_round(f32))
@@ -257,3 +264,55 @@ def test_absolute_positions_clamp_past_max(be, oracle_mod, dtype):
     want = oracle_mod.forward(cfg, blob, ids, lens)
     got = model(be, cfg, dtype, 3).forward_batch(ids, lens, 1)
     (assert_close_f32 if dtype == "f32" else assert_close_16)(got, want["mean"], f"{dtype} clamp")
+
+
+@pytest.mark.parametrize("file_dtype,model_dtype", [("BF16", "bf16"), ("F32", "bf16"), ("F16", "f16"), ("F32", "f32")])
+def test_direct_16bit_checkpoint_ingest(be, tmp_path, file_dtype, model_dtype):
+    """Cuda_Model_LoadTensor takes each SafeTensors tensor in its stored dtype, (out, in) Linear
+    weights included, with no host fp32 blob: the model it builds is bit-identical (same
+    outputs) to LoadRaw of the host-widened blob.  fp16 is compared under IEEE conversion,
+    because the reference's fp16 conversion of the widened blob would flush the file's
+    subnormals that a direct fp16 copy keeps."""
+    import fletcher
+    import weights
+    cfg = dataclasses.replace(synth.NOMIC, num_layers=2, has_bias=True)
+    blob = synth.make_weights(cfg, 21)
+    path = str(tmp_path / f"ckpt_{file_dtype}.safetensors")
+    weights.write_safetensors(path, weights.safetensors_from_blob(blob, cfg), file_dtype)
+    lens = np.array([77, 3, 200], np.int32)
+    ids = synth.make_ids(lens, cfg.vocab_size, 8)
+    if file_dtype == "F16":
+        be.set_half_conversion(fletcher.HALF_RNE)
+    try:
+        direct = fletcher.BertModel(be, cfg, model_dtype)
+        weights.load_safetensors_direct(direct, path)
+        viaraw = fletcher.BertModel(be, cfg, model_dtype)
+        viaraw.load_raw(weights.blob_from_safetensors(path, cfg))
+        for pooling in (0, 1):
+            a = direct.forward_batch(ids, lens, pooling)
+            b = viaraw.forward_batch(ids, lens, pooling)
+            assert np.array_equal(a, b), (pooling, np.abs(a - b).max())
+        direct.close()
+        viaraw.close()
+    finally:
+        be.set_half_conversion(fletcher.HALF_REFERENCE)
+
+
+def test_load_tensor_errors(be):
+    import fletcher
+    cfg = dataclasses.replace(synth.BERT_TINY, num_layers=1)
+    m = fletcher.BertModel(be, cfg, "bf16")
+    with pytest.raises(fletcher.FletcherError, match="not part of this model"):
+        m.load_tensor("encoder.layer.1.attention.self.query.weight", np.zeros((128, 128), np.float32), fletcher.F32)
+    with pytest.raises(fletcher.FletcherError, match="size mismatch"):
+        m.load_tensor("embeddings.LayerNorm.weight", np.zeros(127, np.float32), fletcher.F32)
+    with pytest.raises(fletcher.FletcherError, match="shape mismatch"):
+        m.load_tensor("encoder.layer.0.intermediate.dense.weight", np.zeros((128, 512), np.float32), fletcher.F32,
+                      transposed=True)
+    with pytest.raises(fletcher.FletcherError, match="only Linear weights"):
+        m.load_tensor("embeddings.word_embeddings.weight", np.zeros((128, 30522), np.float32), fletcher.F32,
+                      transposed=True)
+    assert not m.is_loaded()
+    with pytest.raises(fletcher.FletcherError, match="not loaded"):
+        m.forward_batch(np.array([101, 102], np.int32), np.array([2], np.int32))
+    m.close()

@@ -4,7 +4,7 @@ import ctypes
 import numpy as np
 import pytest
 
-from helpers import attention_np, bf16_round, exp_fast_np
+from helpers import attention_np, bf16_round, exp_fast_np, f16_round_ref
 
 pytestmark = pytest.mark.gpu
 
@@ -76,7 +76,7 @@ def test_linear_tensor_core(fl, be, M, K, N, act, dtype):
     dt = fl.DTYPES[dtype]
     tx, tw, tb = be.new_tensor(M, K, x, dt), be.new_tensor(K, N, w, dt), be.new_tensor(1, N, b, dt)
     got = tx.linear(tx, tw, tb, act).to_host()
-    q = bf16_round if dtype == "bf16" else (lambda a: a.astype(np.float16).astype(np.float32))
+    q = bf16_round if dtype == "bf16" else f16_round_ref
     y = q(x).astype(np.float64) @ q(w).astype(np.float64) + q(b)
     if act == 1:
         u = 0.7978846 * (y + 0.044715 * y ** 3)
@@ -164,7 +164,7 @@ def test_flash_attention_varlen(fl, be, lengths, dtype):
     dt = fl.DTYPES[dtype]
     tq, tk, tv = (be.new_tensor(T, H, a, dt) for a in (q, k, v))
     got = tq.attention_varlen(tq, tk, tv, lengths, nh, 0.125).to_host()
-    qq = bf16_round if dtype == "bf16" else (lambda a: a.astype(np.float16).astype(np.float32))
+    qq = bf16_round if dtype == "bf16" else f16_round_ref
     want = attention_np(qq(q), qq(k), qq(v), lengths, nh, 0.125, fast=False)
     assert np.abs(got - want).max() < (3e-2 if dtype == "bf16" else 5e-3)
 
@@ -185,7 +185,7 @@ def test_flash_attention_moving_max(fl, be, dtype):
     dt = fl.DTYPES[dtype]
     tq, tk, tv = (be.new_tensor(T, H, a, dt) for a in (q, k, v))
     got = tq.attention_varlen(tq, tk, tv, lengths, nh, 0.125).to_host()
-    qq = bf16_round if dtype == "bf16" else (lambda a: a.astype(np.float16).astype(np.float32))
+    qq = bf16_round if dtype == "bf16" else f16_round_ref
     want = attention_np(qq(q), qq(k), qq(v), lengths, nh, 0.125, fast=False)
     assert np.isfinite(got).all()
     assert np.abs(got - want).max() < (6e-2 if dtype == "bf16" else 2e-2)

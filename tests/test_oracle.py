@@ -149,3 +149,121 @@ def test_weight_count_matches_layout(oracle_mod):
     for cfg in (synth.BERT_TINY, synth.NOMIC):
         c = synth.to_c(cfg)
         assert oracle_mod.lib().ref_weight_count(ctypes.byref(c)) == synth.weight_count(cfg)
+
+
+# ---- the reference's fp16 host conversion (internal/device/utils.go:13-91), restated in numpy
+# (tests/helpers.py) and pinned here against the reference's own byte KAT and hand-derived values.
+
+def test_half_conversion_restatement_known_answers():
+    from helpers import f16_to_f32_ref, f32_to_f16_ref
+    # internal/device/cast_test.go:11-47: 1.0 -> 0x3c00, -2.0 -> 0xc000
+    assert list(f32_to_f16_ref([1.0, -2.0])) == [0x3C00, 0xC000]
+    cases = [
+        (float("nan"), 0x7E00), (float("inf"), 0x7C00), (float("-inf"), 0xFC00),  # utils.go:15-23
+        (65504.0, 0x7BFF), (70000.0, 0x7BFF), (-1e6, 0xFBFF),  # clamped to +-65504 (utils.go:31-36)
+        (65520.0, 0x7BFF),  # IEEE would round this to Inf
+        (5e-5, 0x0000), (-5e-5, 0x8000), (6.103515625e-05, 0x0400),  # flush below 2^-14 (utils.go:39-48)
+        (0.0, 0x0000), (-0.0, 0x8000),
+        (1.0009765625, 0x3C01), (1.00146484375, 0x3C01),  # truncation: IEEE RNE gives 0x3C02 for the second
+        (0.1, 0x2E66),  # IEEE RNE gives 0x2E66 too (0.1 rounds down)
+        (-0.3333333, 0xB555),
+    ]
+    for x, want in cases:
+        got = int(f32_to_f16_ref(np.array([x], np.float32))[0])
+        assert got == want, (x, hex(got), hex(want))
+    # Float16ToFloat32: subnormals and -0 read as +0; Inf/NaN keep their bits.
+    got = f16_to_f32_ref(np.array([0x0001, 0x83FF, 0x8000, 0x3C00, 0xC000, 0x7C00, 0xFC00, 0x7E00, 0x7BFF], np.uint16))
+    assert list(got.view(np.uint32)[:3]) == [0, 0, 0]
+    assert got[3] == 1.0 and got[4] == -2.0 and np.isposinf(got[5]) and np.isneginf(got[6]) and np.isnan(got[7])
+    assert got[8] == 65504.0
+    # Every normal fp16 survives the round trip bit for bit.
+    h = np.arange(0, 1 << 16, dtype=np.uint32).astype(np.uint16)
+    e = (h >> 10) & 0x1F
+    normal = (e > 0) & (e < 31)
+    assert np.array_equal(f32_to_f16_ref(f16_to_f32_ref(h[normal])), h[normal])
+
+
+# ---- SwiGLU and naive attention known-answer tests of the reference, restated on the oracle.
+
+def _swiglu_kat_expected(data, n, inter):
+    # internal/device/swiglu_test.go:68-77: silu(first half) * second half, float64 exp
+    ref = np.zeros((n, inter), np.float32)
+    for i in range(n):
+        for j in range(inter):
+            x = data[i * 2 * inter + j]
+            y = data[i * 2 * inter + j + inter]
+            sw = np.float32(x / (np.float32(1.0) + np.float32(math.exp(-float(x)))))
+            ref[i, j] = np.float32(sw * y)
+    return ref
+
+
+def test_swiglu_known_answer(oracle_mod):
+    # swiglu_test.go:10-120: X = I(10), W = data (10 x 256), bias 0 -> LinearActivation(SwiGLU).
+    n, inter = 10, 128
+    data = (np.arange(n * inter * 2) % 100).astype(np.float32) / np.float32(10.0)
+    want = _swiglu_kat_expected(data, n, inter)
+    L = oracle_mod.lib()
+    x = np.eye(n, dtype=np.float32)
+    out = np.zeros((n, inter), np.float32)
+    L.ref_linear_activation(fp(x), n, n, fp(data), 2 * inter, None, 4, fp(out))
+    assert np.abs(out - want).max() <= 1e-6  # the reference test allows 0.1 (for its fp16 kernel)
+
+
+def simple_attention_cpu(q, k, v, batch, seq, head_dim, heads, scale):
+    """simpleAttentionCPU (internal/device/attention_test.go:13-68), float32 loops with a float64
+    exp, as the reference writes it."""
+    H = head_dim * heads
+    out = np.zeros(batch * seq * H, np.float32)
+    for b in range(batch):
+        for h in range(heads):
+            sc = np.zeros(seq * seq, np.float32)
+            for i in range(seq):
+                for j in range(seq):
+                    s = np.float32(0)
+                    for d in range(head_dim):
+                        s = np.float32(s + np.float32(q[b * seq * H + i * H + h * head_dim + d] *
+                                                      k[b * seq * H + j * H + h * head_dim + d]))
+                    sc[i * seq + j] = np.float32(s * np.float32(scale))
+            for i in range(seq):
+                mx = np.float32(-np.finfo(np.float32).max)
+                for j in range(seq):
+                    mx = max(mx, sc[i * seq + j])
+                tot = np.float32(0)
+                for j in range(seq):
+                    e = np.float32(math.exp(float(np.float32(sc[i * seq + j] - mx))))
+                    sc[i * seq + j] = e
+                    tot = np.float32(tot + e)
+                for j in range(seq):
+                    sc[i * seq + j] = np.float32(sc[i * seq + j] / tot)
+            for i in range(seq):
+                for d in range(head_dim):
+                    s = np.float32(0)
+                    for j in range(seq):
+                        s = np.float32(s + np.float32(sc[i * seq + j] * v[b * seq * H + j * H + h * head_dim + d]))
+                    out[b * seq * H + i * H + h * head_dim + d] = s
+    return out
+
+
+def attention_kat_inputs():
+    # attention_test.go:71-93: batch 1, seq 4, 2 heads of 4, q = i*0.1, k = (n-i)*0.1, v = (i%3)*0.5
+    batch, seq, heads, hd = 1, 4, 2, 4
+    n = batch * seq * heads * hd
+    i = np.arange(n)
+    q = (i.astype(np.float32) * np.float32(0.1)).astype(np.float32)
+    k = ((n - i).astype(np.float32) * np.float32(0.1)).astype(np.float32)
+    v = ((i % 3).astype(np.float32) * np.float32(0.5)).astype(np.float32)
+    return q, k, v, batch, seq, heads, hd, np.float32(1.0 / math.sqrt(hd))
+
+
+def test_attention_known_answer(oracle_mod):
+    q, k, v, batch, seq, heads, hd, scale = attention_kat_inputs()
+    want = simple_attention_cpu(q, k, v, batch, seq, hd, heads, scale)
+    L = oracle_mod.lib()
+    out = np.zeros_like(q)
+    lens = np.array([seq] * batch, np.int32)
+    L.ref_attention(fp(q), fp(k), fp(v), fp(out), heads * hd, heads, lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                    batch, float(scale))
+    mse = float(((out.astype(np.float64) - want) ** 2).mean())
+    assert mse <= 1e-3  # the reference's bound (attention_test.go:121-124)
+    # The oracle uses ExpFast where the KAT uses float64 exp: well inside ExpFast's error.
+    assert np.abs(out - want).max() <= 5e-3

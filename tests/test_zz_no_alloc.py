@@ -45,6 +45,19 @@ def test_no_alloc_matches_allocating_entry_point(fl, dtype, H, heads):
         want = _run(fl, be, "Cuda_Attention_VarLen", q, k, v, lengths, heads, 0.125, dt)
         got = _run(fl, be, "Cuda_Attention_VarLen_NoAlloc", q, k, v, lengths, heads, 0.125, dt)
         np.testing.assert_allclose(got, want, rtol=0, atol=0)
+        # The property the entry point exists for: the call itself allocates nothing (the
+        # context's device-allocation counter is unchanged across it).
+        T, H_ = q.shape
+        tq, tk, tv = (be.new_tensor(T, H_, a, dt) for a in (q, k, v))
+        out = be.new_tensor(T, H_, None, dt)
+        lens = np.ascontiguousarray(lengths, np.int32)
+        before = be.vram_usage()[0]
+        be.check(fl.lib().Cuda_Attention_VarLen_NoAlloc(be.ctx, tq.buf, tk.buf, tv.buf, out.buf,
+                                                        lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                                        lens.size, H_, heads, ctypes.c_float(0.125)))
+        be.synchronize()
+        assert be.vram_usage()[0] == before
+        np.testing.assert_allclose(out.to_host(), want, rtol=0, atol=0)
     be.close()
 
 
