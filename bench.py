@@ -38,9 +38,13 @@ sys.path[:0] = [os.path.join(ROOT, "longbow-fletcher_b200")]
 import synth  # noqa: E402
 
 METRIC = "embeddings/sec (nomic-embed-text seq512 bf16)"
-# ncu-measured DRAM traffic (read + write) of the four tensor-core GEMMs of one nomic layer, per
-# token (profiles/gemm_tc_cfg3.md: 1680 MB for 65.6K tokens).  Scaled to the timed forwards.
+# DRAM traffic (ncu dram__bytes_read.sum + dram__bytes_write.sum) of the four tensor-core GEMMs
+# of one nomic layer, per token, from one capture of a cfg3 forward; scaled to the timed
+# forwards.  Not measured per run (a bench run is never profiled); GEMM_TRAFFIC_NOTE names the
+# capture it comes from.
 GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 25625.0
+GEMM_TRAFFIC_NOTE = ("ncu dram bytes per token per layer of the 4 GEMMs (1680 MB for 65.6K tokens, one cfg3 "
+                     "capture of the GEMM kernel as of commit 780f7e2), scaled to the timed forwards")
 
 
 def peaks():
@@ -140,58 +144,119 @@ def run_reference(args, w, rank):
 
 def run_server_mix(args):
     """cfg5: the server-batcher mix.  Requests of U{1..16} texts with lengths log-uniform in
-    [8, 512] arrive from `clients` closed-loop clients (each submits its next request when the
-    previous one returns); the batcher caps in-flight sequences at 16384 and dispatches batches
-    round-robin to one replica per GPU (embedder.Server).  One process drives all `--gpus` GPUs.
-    Reports sustained vectors/s and per-request latency (submit -> vectors on the host)."""
-    import concurrent.futures as cf
+    [8, 512] go to embedder.Server: the batcher caps the sequences in flight at 16384 and
+    dispatches batches round-robin to one replica per GPU.  One process drives all `--gpus` GPUs.
+
+    Two open-loop passes (arrivals do not wait for earlier requests, so the client count cannot
+    set the throughput):
+      saturation  every request arrives at t=0; the batcher's in-flight cap meters them out, so
+                  vectors/s is the sustained capacity of the replicas;
+      latency     Poisson arrivals at --load x the saturation rate; p50/p99 request latency
+                  (scheduled arrival -> vectors on the host) at that offered load."""
     import threading
 
     import embedder
     cfg = synth.NOMIC
     rng = np.random.default_rng(5)
-    reqs = []
-    for i in range(args.requests):
-        n = int(rng.integers(1, 17))
-        lens = np.exp(rng.uniform(np.log(8), np.log(513), size=n)).astype(np.int32).clip(8, 512)
-        reqs.append((synth.make_ids(lens, cfg.vocab_size, 9000 + i), lens))
-    if args.clients <= 0:
-        args.clients = 256 * args.gpus
+    counts = rng.integers(1, 17, size=args.requests)
+    all_lens = np.exp(rng.uniform(np.log(8), np.log(513), size=int(counts.sum()))).astype(np.int32).clip(8, 512)
+    all_ids = synth.make_ids(all_lens, cfg.vocab_size, 9000)
+    seq_off = np.concatenate([[0], np.cumsum(counts)])
+    tok_off = np.concatenate([[0], np.cumsum(all_lens)])
+    reqs = [(all_ids[tok_off[seq_off[i]]:tok_off[seq_off[i + 1]]], all_lens[seq_off[i]:seq_off[i + 1]])
+            for i in range(args.requests)]
+    nvec = int(counts.sum())
     emb = embedder.Embedder(cfg, synth.make_weights(cfg, 1), devices=range(args.gpus), dtype="bf16",
                             max_tokens=args.max_tokens or None)
     srv = embedder.Server(emb, max_in_flight=16384)
-    for r in reqs[:64]:  # warm-up: workspaces, kernels
+    for r in reqs[:256]:  # warm-up: workspaces, kernels
         srv.submit(*r).result()
-    lat, nxt, lock = [], [0], threading.Lock()
 
-    def client():
-        while True:
-            with lock:
-                i = nxt[0]
-                nxt[0] += 1
-            if i >= len(reqs):
-                return
-            _, t = srv.submit(*reqs[i]).result()
-            lat.append(t)
+    def run(arrivals):
+        futs = [None] * len(reqs)
+        t0 = time.perf_counter()
 
-    t0 = time.perf_counter()
-    with cf.ThreadPoolExecutor(args.clients) as ex:
-        for f in [ex.submit(client) for _ in range(args.clients)]:
-            f.result()
-    wall = time.perf_counter() - t0
+        def submitter():
+            for i, (ids, lens) in enumerate(reqs):
+                at = t0 + arrivals[i]
+                d = at - time.perf_counter()
+                if d > 0.0005:
+                    time.sleep(d)
+                futs[i] = srv.submit(ids, lens, arrival=max(at, t0))
+        th = threading.Thread(target=submitter)
+        th.start()
+        th.join()
+        lat = np.array([f.result()[1] for f in futs]) * 1000
+        wall = time.perf_counter() - t0
+        return nvec / wall, wall, lat
+
+    sat, sat_wall, sat_lat = run(np.zeros(len(reqs)))
+    rate = args.load * sat * len(reqs) / nvec  # requests/s offered in the latency pass
+    gaps = np.random.default_rng(11).exponential(1.0 / rate, len(reqs))
+    lat_v, lat_wall, lat = run(np.cumsum(gaps) - gaps[0])
     srv.close()
     emb.close()
-    nvec = sum(len(r[1]) for r in reqs)
-    lat_ms = np.array(lat) * 1000
     print(json.dumps({
-        "metric": "sustained embeddings/sec, server-batcher mix (nomic-embed-text bf16)", "value": nvec / wall,
+        "metric": "sustained embeddings/sec, server-batcher mix (nomic-embed-text bf16)", "value": sat,
         "unit": "vectors/s", "n_gpus": args.gpus, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "cfg5: requests of U{1..16} texts, lengths log-uniform [8,512], <=16384 sequences "
-                               "in flight, round-robin over per-GPU replicas",
-                   "requests": args.requests, "clients": args.clients, "vectors": nvec,
-                   "max_batch": emb.max_batch, "max_tokens": emb.max_tokens},
-        "latency_ms": {"p50": float(np.percentile(lat_ms, 50)), "p99": float(np.percentile(lat_ms, 99))},
-        "wall_s": wall}), flush=True)
+                               "in flight, round-robin over per-GPU replicas, open-loop arrivals",
+                   "requests": args.requests, "vectors": nvec, "max_batch": emb.max_batch,
+                   "max_tokens": emb.max_tokens},
+        "saturation": {"vectors_per_s": sat, "wall_s": sat_wall, "p50_ms": float(np.percentile(sat_lat, 50)),
+                       "p99_ms": float(np.percentile(sat_lat, 99)),
+                       "note": "all requests arrive at t=0: latency here is queueing behind the backlog"},
+        "latency": {"offered_load": args.load, "offered_requests_per_s": rate, "vectors_per_s": lat_v,
+                    "wall_s": lat_wall, "p50_ms": float(np.percentile(lat, 50)),
+                    "p99_ms": float(np.percentile(lat, 99))}}), flush=True)
+
+
+def run_ops_route(args, w):
+    """--route ops: the reference's model code run unchanged through the op-level C ABI
+    (bert_ops.OpsBertModel: one ABI call per device.Tensor call of bert.go, the ragged-batch
+    fallback included), host ids in and host vectors out, wall-clocked per step."""
+    import torch
+
+    import bert_ops
+    import fletcher as fl
+    be = fl.Backend(0, w.dtype)
+    m = bert_ops.OpsBertModel(be, w.cfg, synth.make_weights(w.cfg, w.seed), fl.DTYPES[w.dtype])
+    batches = []
+    for ids, lens in make_batches(w, 4, 0, 500):
+        # bert.go rotates batch * lengths[0] rows for RoPE (cpu_backend.go:765); with a longer
+        # first sequence that passes the packed rows and the reference panics.  The shortest
+        # sequence goes first: the same work, on a batch the reference can run.
+        k = int(np.argmin(lens))
+        starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
+        order = [k] + [i for i in range(len(lens)) if i != k]
+        ids = np.concatenate([ids[starts[i]:starts[i] + lens[i]] for i in order]).astype(np.int32)
+        batches.append((ids, lens[order]))
+    for i in range(args.warmup):
+        m.forward_batch(*batches[i % 4], fl.POOL_MEAN_L2)
+    be.synchronize()
+    l0 = be.launch_count()
+    with Clocks(0) as clk:
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            m.forward_batch(*batches[i % 4], fl.POOL_MEAN_L2)
+        wall = time.perf_counter() - t0
+    seqs = sum(len(batches[i % 4][1]) for i in range(args.steps))
+    tokens = sum(int(batches[i % 4][1].sum()) for i in range(args.steps))
+    v = seqs / wall
+    print(json.dumps({
+        "metric": METRIC, "route": "ops", "value": v, "unit": "vectors/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": wall * 1000 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {w.name}, lengths {w.dist} [{w.len_lo},{w.len_hi}], bert.go's op "
+                               "sequence through the tensor ABI (ragged batches take its per-sequence fallback; "
+                               "shortest sequence first, so the reference's RoPE stays inside the batch)",
+                   "global_batch": w.batch, "seq_len": w.len_hi},
+        "e2e": {"value": v, "unit": "vectors/s", "h2d_bytes_per_step": tokens * 4 // args.steps,
+                "d2h_bytes_per_step": w.batch * w.cfg.hidden * 4},
+        "gpu_launches": be.launch_count() - l0, "clocks": clk.summary()}), flush=True)
+    del m
+    be.close()
+    del torch
 
 
 def main():
@@ -201,14 +266,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="fletcher", choices=["fletcher", "reference"])
     ap.add_argument("--workload", default="cfg3", choices=sorted(synth.WORKLOADS) + ["cfg5"])
+    ap.add_argument("--route", default="model", choices=["model", "ops"],
+                    help="model: the fused whole-model entry point; ops: bert.go op by op through the tensor ABI")
     ap.add_argument("--ref-sample", type=int, default=4, help="sequences per step for the CPU reference")
     ap.add_argument("--cpu-sample", type=int, default=24, help="sequences in the cpu_baseline sample (~15 s of CPU work at cfg3)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--gather", action="store_true",
                     help="N>1: all-gather every step's pooled vectors to all ranks over NCCL inside the timed region")
     ap.add_argument("--lat-iters", type=int, default=50, help="single-request latency samples")
-    ap.add_argument("--requests", type=int, default=20000, help="cfg5: requests in the sample")
-    ap.add_argument("--clients", type=int, default=0, help="cfg5: concurrent closed-loop clients (default 256 per GPU)")
+    ap.add_argument("--requests", type=int, default=500000, help="cfg5: requests in the stream")
+    ap.add_argument("--load", type=float, default=0.8, help="cfg5: offered load of the latency pass, x saturation")
     ap.add_argument("--max-tokens", type=int, default=0, help="cfg5: token budget per device batch (default: by VRAM)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -224,11 +291,19 @@ def main():
     if args.impl == "reference":
         run_reference(args, w, rank)
         return
+    if args.route == "ops":
+        if rank == 0:
+            run_ops_route(args, w)
+        return
 
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(local)
     if world > 1:
+        # NCCL's communicator set-up lines (ranks, transport) go to stderr for the record; the
+        # communicator carries only the barrier and the max-over-ranks of the timings.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     import fletcher as fl
 
@@ -307,13 +382,15 @@ def main():
     gemm_launches = sum(st[s][1] for s in gemm_stages)
     sustained, burst, hbm, src = peaks()
     achieved = gemm_flops / gemm_launches / (gemm_ms / gemm_launches / 1000) / 1e12
+    # The GEMMs run inside a ~16 ms step and the timed region lasts well under a second, so the
+    # burst peak is the denominator; the sustained (seconds-long, power-capped) figure is beside it.
     roofline = {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05, all 4 GEMMs of every layer)",
-                "achieved": achieved, "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
-                "peak_source": f"{src} bf16_tflops_sustained",
+                "achieved": achieved, "peak": burst, "unit": "TFLOP/s", "frac": achieved / burst,
+                "peak_source": f"{src} bf16_tflops (burst)",
+                "peak_sustained": sustained, "frac_of_sustained": achieved / sustained,
                 "traffic": (GEMM_DRAM_BYTES_PER_TOKEN_LAYER * tok_ns * L / gemm_launches
                             if cfg.hidden == 768 else None),
-                "traffic_note": "ncu dram__bytes_read+write per GEMM launch (profiles/gemm_tc_cfg3.md), "
-                                "per-token figure scaled to the timed forwards",
+                "traffic_note": GEMM_TRAFFIC_NOTE,
                 # activations in + out of the 4 GEMMs: reads 5H + I, writes 5H + I per token (16-bit)
                 "algorithmic_bytes_per_launch": 2.0 * tok_ns * L * (10 * Hh + 2 * I) / gemm_launches,
                 "flops_per_launch": gemm_flops / gemm_launches, "ms_per_launch": gemm_ms / gemm_launches}

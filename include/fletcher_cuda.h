@@ -323,8 +323,12 @@ enum {
 };
 int32_t Cuda_Model_SetStageTiming(CudaModelRef model, int32_t enable);
 int32_t Cuda_Model_StageTimes(CudaModelRef model, float* ms, int64_t* launches, int32_t n);
-/* Copies the last hidden state [sum(lengths), hidden] of the previous forward as float32. */
+/* Copies the last hidden state [sum(lengths), hidden] of the previous forward as float32.  A
+ * mean-pooled forward of a 16-bit model normalises its final rows inside the pooling kernel and
+ * does not store them: LastHidden then fails unless Cuda_Model_SetKeepHidden(model, 1) was set
+ * before that forward (which keeps the separate final LayerNorm pass). */
 int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count);
+int32_t Cuda_Model_SetKeepHidden(CudaModelRef model, int32_t enable);
 int32_t Cuda_Model_Free(CudaModelRef model);
 
 #if defined(__GNUC__)

@@ -23,6 +23,7 @@
 // TMEM per slot: S/P 64 columns + O 64 columns; 256 per CTA.  ~98 KB smem.  All mbarrier waits
 // are bounded (device error flag + abort, as in the GEMM).  No multicast.
 #include <atomic>
+
 #include "tc_common.cuh"
 
 namespace fl {
@@ -30,18 +31,29 @@ namespace tca {
 
 using namespace tc;
 
-constexpr int BQ = 128, BKV = 64, D = 64;
-constexpr int kSlots = 2;
-constexpr int kThreads = 64 + kSlots * 128;
+constexpr int BQ = 128, D = 64;
 constexpr int Q_BYTES = BQ * D * 2;
-constexpr int KV_BYTES = BKV * D * 2;
-// Per slot: Q, K[2], V[2] (each 1024-byte aligned).
-constexpr int SLOT_Q = 0, SLOT_K = Q_BYTES, SLOT_V = Q_BYTES + 2 * KV_BYTES;
-constexpr int SLOT_BYTES = Q_BYTES + 4 * KV_BYTES;
 constexpr int kBarsPerSlot = 11;
-constexpr int OFF_BAR = kSlots * SLOT_BYTES;
-constexpr int SMEM = OFF_BAR + kSlots * kBarsPerSlot * 8 + 16 + 1024;
-constexpr int TMEM_COLS = 256;  // slot s: S [128s, 128s+64) with P in its upper 32 columns, O [128s+64, 128s+128)
+
+// Kernel shape: BKV keys per block, SLOTS query-tile slots per CTA, two CTAs per SM.
+//   BKV = 64,  SLOTS = 2: per slot S 64 columns (P over its upper 32), O 64 -> 4 slots per SM;
+//   BKV = 128, SLOTS = 1: per slot S 128 columns (P over its upper 64), O 64 -> 2 slots per SM,
+//     every MMA at N = 128 (full rate) for S and twice the softmax work per round trip.
+template <int BKV_, int SLOTS_>
+struct AttnCfg {
+  static constexpr int BKV = BKV_, SLOTS = SLOTS_;
+  static constexpr int kThreads = 32 * SLOTS + 128 * SLOTS;
+  static constexpr int KV_BYTES = BKV * D * 2;
+  // Per slot: Q, K[2], V[2] (each 1024-byte aligned).
+  static constexpr int SLOT_Q = 0, SLOT_K = Q_BYTES, SLOT_V = Q_BYTES + 2 * KV_BYTES;
+  static constexpr int SLOT_BYTES = Q_BYTES + 4 * KV_BYTES;
+  static constexpr int OFF_BAR = SLOTS * SLOT_BYTES;
+  static constexpr int SMEM = OFF_BAR + SLOTS * kBarsPerSlot * 8 + 16 + 1024;
+  // TMEM per slot: S [0, BKV) with P (16-bit pairs) over its upper half, O [BKV, BKV + 64).
+  static constexpr int SLOT_COLS = BKV + D;
+  static constexpr int TMEM_COLS = 256;
+  static_assert(SLOTS * SLOT_COLS <= TMEM_COLS, "TMEM columns");
+};
 
 struct AttnArgs {
   const int32_t* cu;
@@ -98,22 +110,22 @@ __device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1) {
       : "f"(a0), "f"(a1));
 }
 // Keys at and past `valid` lie outside the sequence.
-__device__ __forceinline__ void mask_tail(float (&sv)[BKV], int valid) {
+template <int N>
+__device__ __forceinline__ void mask_tail(float (&sv)[N], int valid) {
 #pragma unroll
-  for (int i = 0; i < BKV; i++)
+  for (int i = 0; i < N; i++)
     if (i >= valid) sv[i] = -INFINITY;
 }
 // Row max as a short tree of 3-input max instructions.
-__device__ __forceinline__ float row_max(const float (&sv)[BKV]) {
+template <int N>
+__device__ __forceinline__ float row_max(const float (&sv)[N]) {
   float mp[8];
 #pragma unroll
-  for (int k = 0; k < 8; k++) mp[k] = max3(sv[k], sv[8 + k], sv[16 + k]);
+  for (int k = 0; k < 8; k++) mp[k] = fmaxf(sv[k], sv[8 + k]);
 #pragma unroll
-  for (int k = 0; k < 8; k++) mp[k] = max3(mp[k], sv[24 + k], sv[32 + k]);
+  for (int c = 16; c + 16 <= N; c += 16)
 #pragma unroll
-  for (int k = 0; k < 8; k++) mp[k] = max3(mp[k], sv[40 + k], sv[48 + k]);
-#pragma unroll
-  for (int k = 0; k < 8; k++) mp[k] = fmaxf(mp[k], sv[56 + k]);
+    for (int k = 0; k < 8; k++) mp[k] = max3(mp[k], sv[c + k], sv[c + 8 + k]);
   return max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
 }
 
@@ -124,12 +136,12 @@ __device__ __forceinline__ float kPMax() {
   return std::is_same<T, __nv_bfloat16>::value ? 18446744073709551616.0f : 32768.0f;
 }
 
-// P = 2^(S * scale * log2 e - ms) for a 64-key row: 16-bit pairs in pk, fp32 sum in `sum`.
-template <typename T>
-__device__ __forceinline__ void exp_row(float (&sv)[BKV], float sl2, float ms, uint32_t (&pk)[32], float& sum) {
+// P = 2^(S * scale * log2 e - ms) for an N-key row: 16-bit pairs in pk, fp32 sum in `sum`.
+template <typename T, int N>
+__device__ __forceinline__ void exp_row(float (&sv)[N], float sl2, float ms, uint32_t (&pk)[N / 2], float& sum) {
   float ra[4][2] = {};  // four independent packed partial sums
 #pragma unroll
-  for (int i = 0; i < BKV; i += 2) {
+  for (int i = 0; i < N; i += 2) {
     fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
     sv[i] = ex2(sv[i]);
     sv[i + 1] = ex2(sv[i + 1]);
@@ -139,6 +151,26 @@ __device__ __forceinline__ void exp_row(float (&sv)[BKV], float sl2, float ms, u
   sum = ((ra[0][0] + ra[0][1]) + (ra[1][0] + ra[1][1])) + ((ra[2][0] + ra[2][1]) + (ra[3][0] + ra[3][1]));
 }
 
+// A row of N fp32 S columns (N = 64 or 128) with one wait.
+template <int N>
+__device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[N]) {
+  if constexpr (N == 64) {
+    tmem_ld64(taddr, v);
+  } else {
+    static_assert(N == 128, "row width");
+    float (&a)[64] = *reinterpret_cast<float(*)[64]>(&v[0]);
+    float (&b)[64] = *reinterpret_cast<float(*)[64]>(&v[64]);
+    tmem_ld64x2(taddr, taddr + 64, a, b);
+  }
+}
+// P row (N/2 packed columns).
+template <int N>
+__device__ __forceinline__ void tmem_st_p(uint32_t taddr, const uint32_t (&pk)[N / 2]) {
+#pragma unroll
+  for (int c = 0; c < N / 64; c++) tmem_st32(taddr + 32 * c, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32 * c]));
+}
+
+template <int BKV>
 __device__ __forceinline__ Work decode(const AttnArgs& a, int w) {
   const int2 t = a.tiles[w / a.nh];
   Work r;
@@ -162,10 +194,14 @@ __device__ __forceinline__ uint64_t sw128_desc_mn(uint32_t saddr) {
   return d;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 2)
+template <typename T, int BKV_, int SLOTS_>
+__global__ void __launch_bounds__(AttnCfg<BKV_, SLOTS_>::kThreads, 2)
     k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
               const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
+  using C = AttnCfg<BKV_, SLOTS_>;
+  constexpr int BKV = C::BKV, kSlots = C::SLOTS, KV_BYTES = C::KV_BYTES;
+  constexpr int SLOT_Q = C::SLOT_Q, SLOT_K = C::SLOT_K, SLOT_V = C::SLOT_V, SLOT_BYTES = C::SLOT_BYTES;
+  constexpr int OFF_BAR = C::OFF_BAR, TMEM_COLS = C::TMEM_COLS, SLOT_COLS = C::SLOT_COLS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -217,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int s = warp;
       SlotBars B(bars + s * kBarsPerSlot);
       uint8_t* sb = smem + s * SLOT_BYTES;
-      const uint32_t t_s = tmem + s * 128, t_p = t_s + 32, t_o = t_s + 64;
+      const uint32_t t_s = tmem + s * SLOT_COLS, t_p = t_s + BKV / 2, t_o = t_s + BKV;
       const uint32_t id_s = idesc<T, BQ, BKV>();
       const uint32_t id_o = idesc<T, BQ, D, true>();
       uint32_t gl = 0, gc = 0, gs = 0;  // K/V blocks loaded, K/V blocks consumed, S blocks
@@ -251,14 +287,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       };
       int w = blockIdx.x * kSlots + s;
       if (w < args.num_work) {
-        Work cur = decode(args, w);
+        Work cur = decode<BKV>(args, w);
         int nl = 1;  // blocks of `cur` whose loads were issued
         bool ok = load_q(cur, 0) && load_kv(cur, 0);
         for (uint32_t t = 0; ok; t++) {
           const int wn = w + vstride;
           const bool has_next = wn < args.num_work;
           Work nxt{};
-          if (has_next) nxt = decode(args, wn);
+          if (has_next) nxt = decode<BKV>(args, wn);
           if (!mbar_wait(B.q_full, t & 1, abort, args.err)) break;
           qw++;
           if (!issue_s()) break;
@@ -302,20 +338,20 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
   } else {
-    const int s = (warp - 2) >> 2;
-    const int q = warp & 3;
+    const int s = (warp - kSlots) >> 2;
+    const int q = warp & 3;  // a warp reaches TMEM lanes 32 * (warp id % 4) ..
     const int r = q * 32 + lane;  // query row within the tile
     SlotBars B(bars + s * kBarsPerSlot);
-    const uint32_t t_s = tmem + ((uint32_t)(q * 32) << 16) + s * 128, t_p = t_s + 32, t_o = t_s + 64;
+    const uint32_t t_s = tmem + ((uint32_t)(q * 32) << 16) + s * SLOT_COLS, t_p = t_s + BKV / 2, t_o = t_s + BKV;
     const float sl2 = args.sl2;
     uint32_t gs = 0, t = 0;
     int w = blockIdx.x * kSlots + s;
     Work nxt{};
-    if (w < args.num_work) nxt = decode(args, w);
+    if (w < args.num_work) nxt = decode<BKV>(args, w);
     for (; w < args.num_work; w += vstride, ++t) {
       const Work wk = nxt;
       // The next item's descriptor is fetched now; its loads complete during this item.
-      if (w + vstride < args.num_work) nxt = decode(args, w + vstride);
+      if (w + vstride < args.num_work) nxt = decode<BKV>(args, w + vstride);
       float m_ref = 0.f, l = 0.f;
       bool ok = true;
       // A warp whose 32 query rows all lie past the sequence end (the tail of its last tile)
@@ -334,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           continue;
         }
         float sv[BKV];
-        tmem_ld64(t_s, sv);
+        tmem_ld_row<BKV>(t_s, sv);
         const int valid = wk.L - j * BKV;  // keys of this block inside the sequence (>= 1)
         if (valid < BKV) mask_tail(sv, valid);
         // P against the current reference max (for block 0: the row's first key, which is never
@@ -342,8 +378,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         // afterwards through the largest P.
         if (j == 0) m_ref = sv[0];
         float rsum;
-        uint32_t pk[32];
-        exp_row<T>(sv, sl2, m_ref * sl2, pk, rsum);
+        uint32_t pk[BKV / 2];
+        exp_row<T, BKV>(sv, sl2, m_ref * sl2, pk, rsum);
         // The row sum bounds every P of the row, so a sum within the P range proves that no P
         // left it (a NaN fails the test too).  A sum beyond the range with every P inside it only
         // costs a needless rescale.
@@ -352,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           // Rare path: some row's max moved by more than the P range allows.  S is still in
           // TMEM (P is not written yet); O holds PV_0..PV_{j-1} complete (S_j's commit came
           // after PV_{j-1}).
-          tmem_ld64(t_s, sv);
+          tmem_ld_row<BKV>(t_s, sv);
           if (valid < BKV) mask_tail(sv, valid);
           const float mx = row_max(sv);
           float f = 1.0f;
@@ -372,11 +408,11 @@ __global__ void __launch_bounds__(kThreads, 2)
               tmem_st32(t_o + hh * 32, ou);
             }
           }
-          tmem_ld64(t_s, sv);
+          tmem_ld_row<BKV>(t_s, sv);
           if (valid < BKV) mask_tail(sv, valid);
-          exp_row<T>(sv, sl2, m_ref * sl2, pk, rsum);
+          exp_row<T, BKV>(sv, sl2, m_ref * sl2, pk, rsum);
         }
-        tmem_st32(t_p, pk);
+        tmem_st_p<BKV>(t_p, pk);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(B.p_full);
@@ -431,6 +467,33 @@ __global__ void __launch_bounds__(kThreads, 2)
 int32_t make_tma_map_2d(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, uint64_t rows, uint64_t cols,
                         uint64_t ld, uint32_t box_cols, uint32_t box_rows);
 
+template <typename T, int BKV, int SLOTS>
+static int32_t launch_attn_variant(Ctx* c, int32_t dt, const void* q, const void* k, const void* v, int64_t ld_in,
+                                   int64_t T_, int64_t H, void* out, int64_t ld_out, const int32_t* cu,
+                                   const int2* tiles128, int32_t num_tiles, int32_t nh, float scale) {
+  using namespace tca;
+  using C = AttnCfg<BKV, SLOTS>;
+  CUtensorMap mq, mk, mv;
+  int32_t rc;
+  if ((rc = make_tma_map_2d(c, &mq, dt, q, (uint64_t)T_, (uint64_t)H, (uint64_t)ld_in, D, BQ))) return rc;
+  if ((rc = make_tma_map_2d(c, &mk, dt, k, (uint64_t)T_, (uint64_t)H, (uint64_t)ld_in, D, BKV))) return rc;
+  if ((rc = make_tma_map_2d(c, &mv, dt, v, (uint64_t)T_, (uint64_t)H, (uint64_t)ld_in, D, BKV))) return rc;
+  const int work = num_tiles * nh;
+  const int st256 = ((uintptr_t)out & 31) == 0 && (ld_out * 2) % 32 == 0;
+  AttnArgs a{cu, tiles128, work, nh, out, ld_out, scale * 1.4426950408889634f, c->d_err, st256};
+  // Per device; host threads of several replicas may get here at once (idempotent).
+  static std::atomic<bool> attr_set[64] = {};
+  if (!attr_set[c->device & 63].load(std::memory_order_acquire)) {
+    FL_CUDA(c, cudaFuncSetAttribute(k_attn_tc<T, BKV, SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_set[c->device & 63].store(true, std::memory_order_release);
+  }
+  const int want = (work + SLOTS - 1) / SLOTS;
+  const int grid = want < 2 * c->num_sms ? want : 2 * c->num_sms;
+  FL_CUDA(c, launch_pdl(k_attn_tc<T, BKV, SLOTS>, dim3(grid), dim3(C::kThreads), C::SMEM, c->stream, mq, mk, mv, a));
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
 int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void* k, const void* v, int64_t ld_in,
                                   int64_t T, int64_t H, void* out, int64_t ld_out, const int32_t* cu,
                                   const int2* tiles128, int32_t num_tiles, int32_t nh, float scale) {
@@ -441,32 +504,14 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void*
                   ((uintptr_t)v & 15) == 0 && ((uintptr_t)out & 15) == 0,
            "attention_tc: rows must be 16-byte aligned");
   FL_CHECK(c, (int64_t)num_tiles * nh < (1ll << 31), "attention_tc: too many work items");
-  CUtensorMap mq, mk, mv;
-  int32_t rc;
-  if ((rc = make_tma_map_2d(c, &mq, dt, q, (uint64_t)T, (uint64_t)H, (uint64_t)ld_in, D, BQ))) return rc;
-  if ((rc = make_tma_map_2d(c, &mk, dt, k, (uint64_t)T, (uint64_t)H, (uint64_t)ld_in, D, BKV))) return rc;
-  if ((rc = make_tma_map_2d(c, &mv, dt, v, (uint64_t)T, (uint64_t)H, (uint64_t)ld_in, D, BKV))) return rc;
-  const int work = num_tiles * nh;
-  const int st256 = ((uintptr_t)out & 31) == 0 && (ld_out * 2) % 32 == 0;
-  AttnArgs a{cu, tiles128, work, nh, out, ld_out, scale * 1.4426950408889634f, c->d_err, st256};
-  // Per dtype and device; host threads of several replicas may get here at once (idempotent).
-  static std::atomic<bool> attr_set[2][64] = {};
-  const int ti = dt == FLETCHER_BF16 ? 0 : 1;
-  if (!attr_set[ti][c->device & 63].load(std::memory_order_acquire)) {
-    if (dt == FLETCHER_BF16)
-      FL_CUDA(c, cudaFuncSetAttribute(k_attn_tc<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-    else
-      FL_CUDA(c, cudaFuncSetAttribute(k_attn_tc<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-    attr_set[ti][c->device & 63].store(true, std::memory_order_release);
-  }
-  const int want = (work + kSlots - 1) / kSlots;
-  const int grid = want < 2 * c->num_sms ? want : 2 * c->num_sms;
+  // 64-key blocks, two slots per CTA, two CTAs per SM.  The 128-key, one-slot shape (N = 128
+  // MMAs for S, half the slots per SM) measured slower: 2.70-2.75 against 2.24-2.30 ms of
+  // attention per cfg3 step, A/B on one box at 1.91-1.97 GHz.
   if (dt == FLETCHER_BF16)
-    FL_CUDA(c, launch_pdl(k_attn_tc<__nv_bfloat16>, dim3(grid), dim3(kThreads), SMEM, c->stream, mq, mk, mv, a));
-  else
-    FL_CUDA(c, launch_pdl(k_attn_tc<__half>, dim3(grid), dim3(kThreads), SMEM, c->stream, mq, mk, mv, a));
-  FL_LAUNCH(c);
-  return FLETCHER_OK;
+    return launch_attn_variant<__nv_bfloat16, 64, 2>(c, dt, q, k, v, ld_in, T, H, out, ld_out, cu, tiles128, num_tiles,
+                                                     nh, scale);
+  return launch_attn_variant<__half, 64, 2>(c, dt, q, k, v, ld_in, T, H, out, ld_out, cu, tiles128, num_tiles, nh,
+                                            scale);
 }
 
 }  // namespace fl

@@ -26,6 +26,15 @@ int32_t launch_positions(Ctx* c, const int32_t* cu_seqlens, int32_t B, int32_t* 
 int32_t launch_mean_pool_l2(Ctx* c, int32_t dtype, const void* hidden, const int32_t* cu_seqlens,
                             int32_t B, int64_t H, float* out);
 
+// The final LayerNorm fused into mean pooling + L2 (16-bit models): out[s] = L2(mean over the
+// rows of sequence s of LayerNorm(x[r])), without writing the normalised rows.  ws holds
+// ln_pool_workspace_bytes() of chunk sums.
+bool ln_pool_supported(int32_t dtype, int64_t H);
+int64_t ln_pool_workspace_bytes(int32_t B, int32_t max_len, int64_t H);
+int32_t launch_ln_mean_pool_l2(Ctx* c, int32_t dtype, const void* x, const int32_t* cu, const float* gamma,
+                               const float* beta, float eps, int32_t B, int32_t max_len, int64_t H, float* ws,
+                               float* out);
+
 // Gathers rows rows_idx[i] of src (dtype) into dst fp32 [n, H].
 int32_t launch_gather_rows_f32(Ctx* c, int32_t dtype, const void* src, const int32_t* rows_idx,
                                int64_t n, int64_t H, float* dst);

@@ -64,6 +64,10 @@ struct Model {
   float* d_cls = nullptr;
   float* splitk = nullptr;  // split-K partial sums of the GEMMs of small batches
   int64_t splitk_bytes = 0;
+  float* lnpool = nullptr;  // chunk sums of the last LayerNorm fused into mean pooling
+  int64_t lnpool_bytes = 0;
+  bool keep_hidden = false;  // Cuda_Model_SetKeepHidden: store the final hidden state
+  bool last_fused = false;   // the previous forward fused its final LayerNorm into the pool
   std::vector<std::pair<void*, int64_t>> ws;
   // pinned staging for per-batch metadata
   uint8_t* h_meta = nullptr;
@@ -618,6 +622,18 @@ static int32_t forward_device(Model* m, const int32_t* d_ids, const int32_t* len
   int32_t n_tiles = 0, max_len = 0;
   if ((rc = upload_meta(m, lengths, B, T, &n_tiles, &max_len))) return rc;
   if ((rc = ensure_rope(m, max_len))) return rc;
+  if (m->dtype != FLETCHER_F32 && ln_pool_supported(m->dtype, m->H)) {
+    const int64_t need = ln_pool_workspace_bytes(B, max_len, m->H);
+    if (need > m->lnpool_bytes) {
+      clear_graphs(m);  // captured graphs hold the old pointer
+      if (m->lnpool) dev_free(c, m->lnpool, m->lnpool_bytes);
+      m->lnpool = nullptr;
+      m->lnpool_bytes = 0;
+      const int64_t cap = std::max<int64_t>(need, 1 << 20);
+      if ((rc = dev_alloc(c, (void**)&m->lnpool, cap))) return rc;
+      m->lnpool_bytes = cap;
+    }
+  }
   m->last_T = T;
   c->splitk = m->splitk;  // this model's split-K workspace for its GEMM launches
   c->splitk_bytes = m->splitk_bytes;
@@ -647,7 +663,14 @@ static int32_t run_layers(Model* m, const int32_t* d_ids, int32_t B, int32_t poo
   const int64_t es = dtype_size(dt);
   const float scale = 1.0f / (float)std::sqrt((double)m->dh);
   const bool swiglu = m->cfg.activation == FLETCHER_ACT_SWIGLU;
-  for (auto& L : m->layers) {
+  // Mean pooling of a 16-bit model: the last LayerNorm is fused into the pool, so the final
+  // normalised rows are never written (unless the caller keeps the last hidden state).
+  const bool fuse_last = pooling == FLETCHER_POOL_MEAN_L2 && dt != FLETCHER_F32 && ln_pool_supported(dt, H) &&
+                         !m->keep_hidden && m->lnpool && !m->layers.empty();
+  m->last_fused = fuse_last;
+  for (size_t li = 0; li < m->layers.size(); li++) {
+    auto& L = m->layers[li];
+    const bool last = li + 1 == m->layers.size();
     if (dt == FLETCHER_F32) {
       FL_STAGE(FLETCHER_STAGE_GEMM_QKV, launch_sgemm(c, (float*)m->X, H, (float*)L.wqkv, 3 * H, (float*)m->QKV, 3 * H, T,
                                                      3 * H, H, L.bqkv, FLETCHER_ACT_IDENTITY));
@@ -690,6 +713,11 @@ static int32_t run_layers(Model* m, const int32_t* d_ids, int32_t B, int32_t poo
                                                       Iup, m->ACT, I, L.bi, nullptr, 0, nullptr, nullptr, nullptr, 0));
       FL_STAGE(FLETCHER_STAGE_GEMM_DOWN, launch_gemm_tc(c, dt, EPI_RESIDUAL, m->bn_d, m->ACT, T, I, L.wd, H, m->S, H,
                                                         L.bd, m->X, H, nullptr, nullptr, nullptr, 0));
+      if (last && fuse_last) {
+        FL_STAGE(FLETCHER_STAGE_POOL, launch_ln_mean_pool_l2(c, dt, m->S, m->d_cu, L.ln2g, L.ln2b, eps, B, max_len, H,
+                                                             m->lnpool, d_out));
+        return FLETCHER_OK;
+      }
       FL_STAGE(FLETCHER_STAGE_LAYERNORM, launch_add_layernorm(c, dt, m->S, nullptr, m->X, L.ln2g, L.ln2b, T, H, eps));
     }
   }
@@ -813,6 +841,7 @@ static void destroy(Model* m) {
   for (auto& a : m->allocs) dev_free(c, a.first, a.second);
   if (m->cos_t) dev_free(c, m->cos_t, (int64_t)m->rope_len * (m->dh / 2) * 4);
   if (m->sin_t) dev_free(c, m->sin_t, (int64_t)m->rope_len * (m->dh / 2) * 4);
+  if (m->lnpool) dev_free(c, m->lnpool, m->lnpool_bytes);
   cudaStreamSynchronize(c->stream);
   if (m->h_meta) cudaFreeHost(m->h_meta);
   if (m->meta_done) cudaEventDestroy(m->meta_done);
@@ -978,6 +1007,9 @@ int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count
   Ctx* c = m->c;
   DeviceGuard g(c);
   FL_CHECK(c, count <= m->last_T * m->H, "LastHidden: count exceeds the last batch");
+  FL_CHECK(c, !m->last_fused,
+           "LastHidden: the previous mean-pooled forward fused its final LayerNorm into the pool and did not store "
+           "the hidden state (enable Cuda_Model_SetKeepHidden first)");
   float* tmp = nullptr;
   int32_t rc = dev_alloc(c, (void**)&tmp, count * 4);
   if (rc) return rc;
@@ -989,6 +1021,16 @@ int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count
   dev_free(c, tmp, count * 4);
   FL_CUDA(c, cudaStreamSynchronize(c->stream));
   return rc;
+}
+
+int32_t Cuda_Model_SetKeepHidden(CudaModelRef model, int32_t enable) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m) return FLETCHER_ERR_INVALID;
+  DeviceGuard g(m->c);
+  FL_CUDA(m->c, cudaStreamSynchronize(m->c->stream));
+  m->keep_hidden = enable != 0;
+  clear_graphs(m);  // the kernel sequence changes
+  return FLETCHER_OK;
 }
 
 int32_t Cuda_Model_SetGraphs(CudaModelRef model, int32_t enable) {

@@ -344,6 +344,140 @@ int32_t launch_mean_pool_l2(Ctx* c, int32_t dt, const void* h, const int32_t* cu
   return mean_pool_t<__half>(c, (const __half*)h, cu, B, H, out);
 }
 
+// ---------------------------------------------------------------- LayerNorm fused into mean pool
+// The last layer's LayerNorm and the mean-pool + L2 head in two passes, without writing the
+// normalised [T, H] rows: stage 1 takes a chunk of up to kLnPoolRows rows of one sequence (grid:
+// chunks x sequences; chunks past a sequence's end exit), normalises each row in registers with
+// the LayerNorm kernel's arithmetic (one warp per row, rounded to the model dtype exactly as the
+// LayerNorm kernel stores it) and writes the chunk's fp32 column sums; stage 2 adds a sequence's
+// chunk sums in chunk order, divides by its length and L2-normalises.  Deterministic: the same
+// summation order on every run.
+constexpr int kLnPoolRows = 64, kLnPoolWarps = 8;
+
+template <typename T, int PER, int VEC>
+__global__ void __launch_bounds__(kLnPoolWarps * 32)
+    k_ln_pool_partial(const T* __restrict__ x, const int32_t* __restrict__ cu, const float* __restrict__ g,
+                      const float* __restrict__ b, float eps, int cols, int chunks, float* __restrict__ partial) {
+  pdl_wait();
+  extern __shared__ float red[];  // [kLnPoolWarps][cols]
+  const int sq = blockIdx.y, ch = blockIdx.x;
+  const int a = cu[sq] + ch * kLnPoolRows, e = min(cu[sq + 1], a + kLnPoolRows);
+  if (a >= e) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; i++) acc[i] = 0.f;
+  for (int r = a + warp; r < e; r += kLnPoolWarps) {
+    float v[PER];
+    const T* xr = x + (int64_t)r * cols;
+#pragma unroll
+    for (int j = 0; j < PER / VEC; j++) {
+      Vec<T, VEC> t = *reinterpret_cast<const Vec<T, VEC>*>(xr + (j * 32 + lane) * VEC);
+#pragma unroll
+      for (int i = 0; i < VEC; i++) v[j * VEC + i] = to_f<T>(t.d[i]);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) s += v[i];
+    s = warp_sum(s);
+    const float mean = __fdiv_rn(s, (float)cols);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      float d = __fsub_rn(v[i], mean);
+      q = __fadd_rn(q, __fmul_rn(d, d));
+    }
+    q = warp_sum(q);
+    const float var = __fdiv_rn(q, (float)cols);
+    const float inv = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(var, eps)));
+#pragma unroll
+    for (int j = 0; j < PER / VEC; j++) {
+      const int e0 = (j * 32 + lane) * VEC;
+      Vec<float, VEC> gv = *reinterpret_cast<const Vec<float, VEC>*>(g + e0);
+      Vec<float, VEC> bv = *reinterpret_cast<const Vec<float, VEC>*>(b + e0);
+#pragma unroll
+      for (int i = 0; i < VEC; i++)
+        acc[j * VEC + i] += to_f<T>(
+            from_f<T>(__fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j * VEC + i], mean), inv), gv.d[i]), bv.d[i])));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < PER / VEC; j++)
+#pragma unroll
+    for (int i = 0; i < VEC; i++) red[warp * cols + (j * 32 + lane) * VEC + i] = acc[j * VEC + i];
+  __syncthreads();
+  float* dst = partial + ((int64_t)sq * chunks + ch) * cols;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kLnPoolWarps; w++) t += red[w * cols + c];
+    dst[c] = t;
+  }
+}
+
+__global__ void __launch_bounds__(256) k_ln_pool_finish(const float* __restrict__ partial, const int32_t* __restrict__ cu,
+                                                        int cols, int chunks, float* __restrict__ out) {
+  pdl_wait();
+  extern __shared__ float mean[];  // [cols]
+  __shared__ float red[8];
+  const int sq = blockIdx.x;
+  const int len = cu[sq + 1] - cu[sq];
+  const int nch = (len + kLnPoolRows - 1) / kLnPoolRows;
+  const float invn = len > 0 ? 1.0f / (float)len : 0.f;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float t = 0.f;
+    for (int k = 0; k < nch; k++) t += partial[((int64_t)sq * chunks + k) * cols + c];
+    t *= invn;
+    mean[c] = t;
+    ss += t * t;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += red[i];
+  const float inv = tot > 0.f ? (float)(1.0 / sqrt((double)tot)) : 0.f;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) out[(int64_t)sq * cols + c] = mean[c] * inv;
+}
+
+bool ln_pool_supported(int32_t dt, int64_t H) { return dt != FLETCHER_F32 && (H == 768 || H == 1024 || H == 512 || H == 256); }
+
+int64_t ln_pool_workspace_bytes(int32_t B, int32_t max_len, int64_t H) {
+  return (int64_t)B * ((max_len + kLnPoolRows - 1) / kLnPoolRows) * H * 4;
+}
+
+template <typename T>
+static int32_t ln_pool_t(Ctx* c, const T* x, const int32_t* cu, const float* g, const float* b, float eps, int32_t B,
+                         int32_t max_len, int64_t H, float* ws, float* out) {
+  constexpr int V = 8;  // 16-bit rows: 128-bit loads
+  const int chunks = (max_len + kLnPoolRows - 1) / kLnPoolRows;
+  const dim3 grid((unsigned)chunks, (unsigned)B);
+  const size_t smem = (size_t)kLnPoolWarps * H * 4;
+#define FL_LNP(PER_)                                                                                                 \
+  FL_CUDA(c, launch_pdl(k_ln_pool_partial<T, PER_, V>, grid, dim3(kLnPoolWarps * 32), smem, c->stream, x, cu, g, b, eps, \
+                        (int)H, chunks, ws))
+  if (H == 768) FL_LNP(24);
+  else if (H == 1024) FL_LNP(32);
+  else if (H == 512) FL_LNP(16);
+  else FL_LNP(8);
+#undef FL_LNP
+  FL_LAUNCH(c);
+  FL_CUDA(c, launch_pdl(k_ln_pool_finish, dim3((unsigned)B), dim3(256), (size_t)H * 4, c->stream, (const float*)ws, cu,
+                        (int)H, chunks, out));
+  FL_LAUNCH(c);
+  return FLETCHER_OK;
+}
+
+int32_t launch_ln_mean_pool_l2(Ctx* c, int32_t dt, const void* x, const int32_t* cu, const float* g, const float* b,
+                               float eps, int32_t B, int32_t max_len, int64_t H, float* ws, float* out) {
+  FL_CHECK(c, ln_pool_supported(dt, H), "ln_mean_pool: unsupported dtype/width");
+  if (B <= 0) return FLETCHER_OK;
+  if (dt == FLETCHER_BF16)
+    return ln_pool_t<__nv_bfloat16>(c, (const __nv_bfloat16*)x, cu, g, b, eps, B, max_len, H, ws, out);
+  return ln_pool_t<__half>(c, (const __half*)x, cu, g, b, eps, B, max_len, H, ws, out);
+}
+
 // ---------------------------------------------------------------- gather rows -> f32
 template <typename T>
 __global__ void k_gather_rows_f32(const T* __restrict__ src, const int32_t* __restrict__ idx, int64_t H,

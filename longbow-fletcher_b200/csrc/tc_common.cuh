@@ -236,6 +236,33 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// Two 64-column loads (any columns of this thread's lane) completed by one wait.
+#define FL_TMEM_LD64_ASM(ADDR, R)                                                                                    \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"        \
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,"    \
+               "%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];" \
+               : "=r"(R[0]), "=r"(R[1]), "=r"(R[2]), "=r"(R[3]), "=r"(R[4]), "=r"(R[5]), "=r"(R[6]), "=r"(R[7]),      \
+                 "=r"(R[8]), "=r"(R[9]), "=r"(R[10]), "=r"(R[11]), "=r"(R[12]), "=r"(R[13]), "=r"(R[14]),              \
+                 "=r"(R[15]), "=r"(R[16]), "=r"(R[17]), "=r"(R[18]), "=r"(R[19]), "=r"(R[20]), "=r"(R[21]),            \
+                 "=r"(R[22]), "=r"(R[23]), "=r"(R[24]), "=r"(R[25]), "=r"(R[26]), "=r"(R[27]), "=r"(R[28]),            \
+                 "=r"(R[29]), "=r"(R[30]), "=r"(R[31]), "=r"(R[32]), "=r"(R[33]), "=r"(R[34]), "=r"(R[35]),            \
+                 "=r"(R[36]), "=r"(R[37]), "=r"(R[38]), "=r"(R[39]), "=r"(R[40]), "=r"(R[41]), "=r"(R[42]),            \
+                 "=r"(R[43]), "=r"(R[44]), "=r"(R[45]), "=r"(R[46]), "=r"(R[47]), "=r"(R[48]), "=r"(R[49]),            \
+                 "=r"(R[50]), "=r"(R[51]), "=r"(R[52]), "=r"(R[53]), "=r"(R[54]), "=r"(R[55]), "=r"(R[56]),            \
+                 "=r"(R[57]), "=r"(R[58]), "=r"(R[59]), "=r"(R[60]), "=r"(R[61]), "=r"(R[62]), "=r"(R[63])             \
+               : "r"(ADDR))
+__device__ __forceinline__ void tmem_ld64x2(uint32_t ta, uint32_t tb, float (&a)[64], float (&b)[64]) {
+  uint32_t ra[64], rb[64];
+  FL_TMEM_LD64_ASM(ta, ra);
+  FL_TMEM_LD64_ASM(tb, rb);
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; i++) {
+    a[i] = __uint_as_float(ra[i]);
+    b[i] = __uint_as_float(rb[i]);
+  }
+}
+
 // Non-blocking probe of an mbarrier phase (for threads that poll several pipelines).
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   uint32_t ok;

@@ -196,48 +196,79 @@ class Embedder:
 class Server:
     """Request queue + dynamic batcher + round-robin dispatch to the replicas."""
 
-    def __init__(self, embedder: Embedder, max_in_flight=16384):
+    def __init__(self, embedder: Embedder, max_in_flight=16384, jobs_per_replica=2):
         self.emb = embedder
         self.max_in_flight = max_in_flight
+        # A replica takes a new batch only while it holds fewer than this many: requests that
+        # arrive meanwhile wait and join one larger batch, so batches grow with the load instead
+        # of fragmenting into many small device batches.
+        self.jobs_per_replica = jobs_per_replica
         self.q = queue.Queue()
         self.rr = 0
         self.stop = False
         self.thread = threading.Thread(target=self._loop, daemon=True)
         self.thread.start()
 
-    def submit(self, ids, lengths):
-        """Returns a Future resolving to (vectors [n, H], latency seconds)."""
+    def submit(self, ids, lengths, arrival=None):
+        """Returns a Future resolving to (vectors [n, H], latency seconds).  Latency runs from
+        `arrival` (a time.perf_counter() value, e.g. a request's scheduled arrival in an
+        open-loop load) or from this call."""
         fut = cf.Future()
-        self.q.put((time.perf_counter(), np.asarray(ids, np.int32), np.asarray(lengths, np.int32), fut))
+        t0 = time.perf_counter() if arrival is None else arrival
+        self.q.put((t0, np.asarray(ids, np.int32), np.asarray(lengths, np.int32), fut))
         return fut
 
     def _loop(self):
-        inflight = []  # (replica future, [requests])
-        while not self.stop or not self.q.empty():
-            reqs, nseq = [], 0
-            try:
-                reqs.append(self.q.get(timeout=0.01))
-                nseq = len(reqs[0][2])
-            except queue.Empty:
-                pass
-            while reqs and nseq < self.max_in_flight:
+        """Drains the queue into batches of at most the free in-flight budget (sequences handed to
+        the replicas and not yet returned stay below max_in_flight, as the reference's server
+        semaphore caps them, server.go:101) and dispatches them round-robin."""
+        inflight = []  # (replica future, [requests], sequences, replica index)
+        held = collections.deque()  # requests taken off the queue, not yet dispatched
+        busy = 0
+        nrep = len(self.emb.replicas)
+        jobs = [0] * nrep
+        while not self.stop or not self.q.empty() or held:
+            if not held:
                 try:
-                    r = self.q.get_nowait()
+                    held.append(self.q.get(timeout=0.002 if inflight else 0.01))
+                except queue.Empty:
+                    pass
+            while True:  # everything queued now, so that one batch takes it all
+                try:
+                    held.append(self.q.get_nowait())
                 except queue.Empty:
                     break
+            # The next replica in round-robin order with room for another batch.
+            rep = None
+            for k in range(nrep):
+                i = (self.rr + k) % nrep
+                if jobs[i] < self.jobs_per_replica:
+                    rep = i
+                    break
+            reqs, nseq = [], 0
+            while rep is not None and held and (busy + nseq + len(held[0][2]) <= self.max_in_flight
+                                                or (busy == 0 and not reqs)):
+                r = held.popleft()
                 reqs.append(r)
                 nseq += len(r[2])
             if reqs:
-                rep = self.emb.replicas[self.rr % len(self.emb.replicas)]
-                self.rr += 1
+                self.rr = rep + 1
                 ids = np.concatenate([r[1] for r in reqs])
                 lens = np.concatenate([r[2] for r in reqs])
-                inflight.append((rep.run(ids, lens, self.emb.max_batch, self.emb.max_tokens), reqs))
+                fut = self.emb.replicas[rep].run(ids, lens, self.emb.max_batch, self.emb.max_tokens)
+                inflight.append((fut, reqs, nseq, rep))
+                busy += nseq
+                jobs[rep] += 1
             done = [x for x in inflight if x[0].done()]
-            inflight = [x for x in inflight if not x[0].done()]
-            for f, rq in done:
-                self._finish(f, rq)
-        for f, rq in inflight:
+            if done:
+                inflight = [x for x in inflight if not x[0].done()]
+                for f, rq, n, i in done:
+                    busy -= n
+                    jobs[i] -= 1
+                    self._finish(f, rq)
+            elif inflight and held and not reqs:
+                cf.wait([x[0] for x in inflight], timeout=0.01, return_when=cf.FIRST_COMPLETED)
+        for f, rq, _, _ in inflight:
             self._finish(f, rq)
 
     @staticmethod

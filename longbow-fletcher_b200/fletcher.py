@@ -100,6 +100,7 @@ def _sig(L):
         "Cuda_Model_TensorCount": (i32, [vp]),
         "Cuda_Model_TensorName": (i32, [vp, i32, ctypes.c_char_p, i32]),
         "Cuda_Model_IsLoaded": (i32, [vp]),
+        "Cuda_Model_SetKeepHidden": (i32, [vp, i32]),
         "Cuda_At": (i32, [vp, i64, i64, f32p]),
         "Cuda_Set": (i32, [vp, i64, i64, f32]),
         "Cuda_Copy": (i32, [vp, vp, i64, vp, i64, i64]),
@@ -432,6 +433,9 @@ class BertModel:
 
     STAGES = ["embed", "gemm_qkv", "rope", "attention", "gemm_o", "layernorm", "gemm_up", "activation",
               "gemm_down", "pool"]
+
+    def set_keep_hidden(self, on: bool):
+        self.be.check(lib().Cuda_Model_SetKeepHidden(self.h, int(on)))
 
     def set_graphs(self, on: bool):
         self.be.check(lib().Cuda_Model_SetGraphs(self.h, int(on)))

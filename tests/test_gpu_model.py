@@ -100,9 +100,17 @@ def test_packing_invariance_bitexact(be):
             off += L
 
 
+def _oracle_subset(oracle_mod, cfg, blob, ids, lens, pick):
+    """Spec-mode oracle vectors of the sequences `pick` of a packed batch, in one packed call."""
+    starts = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    sub_ids = np.concatenate([ids[starts[i]:starts[i] + lens[i]] for i in pick]).astype(np.int32)
+    return oracle_mod.forward(cfg, blob, sub_ids, lens[pick])["mean"]
+
+
 def test_cfg3_full_size_bf16(be, oracle_mod):
-    """BASELINE cfg3 at full size (12 layers, B=256, l in [32,512]): finite unit vectors,
-    and a sample of sequences against the oracle."""
+    """BASELINE cfg3 at full size (12 layers, B=256, l in [32,512], seed 1): finite unit vectors,
+    and 64 sequences spread over the length range (every 4th by length, the shortest and the
+    longest included) against the oracle."""
     w = synth.WORKLOADS["cfg3"]
     lens = w.lengths()
     ids = synth.make_ids(lens, w.cfg.vocab_size, w.seed)
@@ -111,11 +119,38 @@ def test_cfg3_full_size_bf16(be, oracle_mod):
     got = m.forward_batch(ids, lens, 1)
     assert np.isfinite(got).all()
     np.testing.assert_allclose(np.linalg.norm(got, axis=1), 1.0, atol=1e-4)
-    starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
-    pick = np.argsort(lens)[[0, 1, len(lens) // 2, -1]]
-    for i in pick:
-        want = oracle_mod.forward(w.cfg, blob, ids[starts[i]:starts[i] + lens[i]], lens[i:i + 1])
-        assert_close_16(got[i:i + 1], want["mean"], f"cfg3 seq {i} len {lens[i]}")
+    order = np.argsort(lens, kind="stable")
+    pick = np.unique(np.concatenate([order[::4], order[-1:]]))
+    assert len(pick) >= 64
+    assert_close_16(got[pick], _oracle_subset(oracle_mod, w.cfg, blob, ids, lens, pick), "cfg3 sample")
+
+
+def test_cfg4_full_depth_long_context_bf16(be, oracle_mod):
+    """BASELINE cfg4 at full depth and size: 12 layers, B=32, l log-uniform in [64, 2048], seed 1,
+    packed varlen.  Every sequence, the longest included, against the oracle."""
+    w = synth.WORKLOADS["cfg4"]
+    lens = w.lengths()
+    assert lens.max() > 1024
+    ids = synth.make_ids(lens, w.cfg.vocab_size, w.seed)
+    blob = synth.make_weights(w.cfg, w.seed)
+    m = model(be, w.cfg, "bf16", w.seed)
+    got = m.forward_batch(ids, lens, 1)
+    assert np.isfinite(got).all()
+    pick = np.arange(len(lens))
+    assert_close_16(got, _oracle_subset(oracle_mod, w.cfg, blob, ids, lens, pick), "cfg4 all 32")
+
+
+def test_cfg2_full_batch_bf16(be, oracle_mod):
+    """BASELINE cfg2: bert-tiny bf16, B=1024, l in [8,128]: every sequence against the oracle, both
+    pooling heads."""
+    w = synth.WORKLOADS["cfg2"]
+    lens = w.lengths()
+    ids = synth.make_ids(lens, w.cfg.vocab_size, w.seed)
+    blob = synth.make_weights(w.cfg, w.seed)
+    want = oracle_mod.forward(w.cfg, blob, ids, lens)
+    m = model(be, w.cfg, "bf16", w.seed)
+    assert_close_16(m.forward_batch(ids, lens, 1), want["mean"], "cfg2 mean")
+    assert_close_16(m.forward_batch(ids, lens, 0), want["cls"], "cfg2 cls")
 
 
 def test_errors_are_reported(be):
@@ -315,4 +350,30 @@ def test_load_tensor_errors(be):
     assert not m.is_loaded()
     with pytest.raises(fletcher.FletcherError, match="not loaded"):
         m.forward_batch(np.array([101, 102], np.int32), np.array([2], np.int32))
+    m.close()
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_final_layernorm_fused_into_pool(be, dtype):
+    """A mean-pooled 16-bit forward normalises its final rows inside the pooling kernels: the
+    vectors equal those of the unfused path (separate LayerNorm pass + pool) up to fp32 summation
+    order, the final hidden state is not stored, and keeping it restores LastHidden."""
+    import fletcher
+    cfg = dataclasses.replace(synth.NOMIC, num_layers=2)
+    m = fletcher.BertModel(be, cfg, dtype)
+    m.load_raw(synth.make_weights(cfg, 4))
+    lens = np.array([1, 64, 65, 200, 513, 7, 130], np.int32)
+    ids = synth.make_ids(lens, cfg.vocab_size, 12)
+    fused = m.forward_batch(ids, lens, fletcher.POOL_MEAN_L2)
+    with pytest.raises(fletcher.FletcherError, match="SetKeepHidden"):
+        m.last_hidden(int(lens.sum()))
+    m.set_keep_hidden(True)
+    plain = m.forward_batch(ids, lens, fletcher.POOL_MEAN_L2)
+    hid = m.last_hidden(int(lens.sum()))
+    assert np.abs(fused - plain).max() <= 2e-6
+    # The unfused path's pool of the stored hidden state, restated in numpy.
+    starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    mean = np.stack([hid[a:a + l].astype(np.float64).mean(0) for a, l in zip(starts, lens)])
+    mean /= np.linalg.norm(mean, axis=1, keepdims=True)
+    assert np.abs(fused - mean).max() <= 2e-6
     m.close()
