@@ -12,8 +12,9 @@ used for the barrier and the max-over-ranks of the device time.
 Printed (rank 0, one JSON line):
   value     vectors/s over all ranks, inputs resident in HBM, device time of K steps (CUDA
             events on the library's stream), max over ranks;
-  e2e       the same metric through the public host entry point Cuda_Model_ForwardBatch with
-            pinned host ids in and host vectors out (H2D + D2H inside the timed region);
+  e2e       the same metric through the public host API (Cuda_Model_ForwardBatchAsync /
+            Cuda_Model_Wait, two batches in flight) with pinned host ids in and host vectors out
+            (every step's H2D + D2H inside the timed region);
   roofline  the tensor-core GEMMs (the dominant kernels): algorithmic FLOPs / their event-timed
             duration, against the measured sustained bf16 peak;
   cpu_baseline  the CPU oracle (C++ restatement of the reference's CPU path, OpenBLAS sgemm)
@@ -398,12 +399,17 @@ def main():
     # HBM-bound kernels: algorithmic bytes of the stage-timing forwards / their event time.
     es = 4 if w.dtype == "f32" else 2
     seqs_ns = sum(len(batches[i % nb][1]) for i in range(ns))
+    # The mean-pooled 16-bit forward fuses the last LayerNorm into the pool (its rows are read
+    # once and never written back).
+    fused = w.dtype != "f32" and cfg.hidden in (256, 512, 768, 1024)
+    n_ln = 2 * L - (1 if fused else 0)
     hbm_bytes = {
-        # LayerNorm (2 per layer): read the residual-stream rows, write the normalised rows.
-        "layernorm": 2.0 * L * tok_ns * Hh * es * 2,
+        # LayerNorm: read the residual-stream rows, write the normalised rows.
+        "layernorm": float(n_ln) * tok_ns * Hh * es * 2,
         # embed: word row (+ position row for absolute positions) read, output row written.
         "embed": tok_ns * Hh * es * (3 if cfg.position_type == synth.POS_ABSOLUTE else 2),
-        # mean-pool + L2: read every token row, write B fp32 vectors.
+        # mean-pool + L2 (with the last LayerNorm when fused): read every token row, write B fp32
+        # vectors.
         "pool": tok_ns * Hh * es + seqs_ns * Hh * 4,
     }
     hbm_kernels = {}
@@ -413,26 +419,29 @@ def main():
             hbm_kernels[k] = {"achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                               "bytes_per_step": nbytes / ns}
 
-    # ---- end to end through the host entry point (pinned host buffers)
-    pin_ids = [torch.from_numpy(ids).pin_memory().numpy() for ids, _ in batches]
-    out_host = torch.empty((w.batch, H), dtype=torch.float32).pin_memory().numpy()
-    import ctypes
-    lib = fl.lib()
+    # ---- end to end through the public host API with host buffers: every step enqueues the H2D
+    # copy of its ids, the forward and the D2H copy of its vectors (Cuda_Model_ForwardBatchAsync,
+    # pinned buffers) and the loop keeps two batches in flight, as a batcher does
+    # (embeddings.go:678-815 waits for each batch; embedder.Replica double-buffers the same way).
+    pin_ids = [torch.from_numpy(ids).pin_memory() for ids, _ in batches]
+    pin_out = [torch.empty((w.batch, H), dtype=torch.float32).pin_memory() for _ in range(2)]
 
-    def e2e_step(i):
-        ids, lens = batches[i % nb]
-        lens = np.ascontiguousarray(lens, np.int32)
-        be.check(lib.Cuda_Model_ForwardBatch(model.h, fl._i32p(pin_ids[i % nb]), fl._i32p(lens), lens.size,
-                                             fl.POOL_MEAN_L2, out_host.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+    def e2e_run(n):
+        tickets = []
+        for i in range(n):
+            ids, lens = batches[i % nb]
+            tickets.append(model.forward_batch_async(pin_ids[i % nb].data_ptr(), lens, fl.POOL_MEAN_L2,
+                                                     pin_out[i % 2].data_ptr()))
+            if i >= 1:
+                model.wait(tickets[i - 1])
+        model.wait(tickets[-1])
 
-    for i in range(2 * nb):  # preparation: capture each shape's graph on this path too
-        e2e_step(i)
+    e2e_run(2 * nb)  # preparation: capture each shape's graph on this path too
     barrier()
     torch.cuda.synchronize()
     e0.record(stream)
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        e2e_step(i)
+    e2e_run(args.steps)
     e1.record(stream)
     e1.synchronize()
     wall = time.perf_counter() - t0

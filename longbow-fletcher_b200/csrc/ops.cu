@@ -78,6 +78,44 @@ __global__ void __launch_bounds__(128) k_add_ln(const T* __restrict__ x, const T
   ln_finish<T, PER, VEC>(v, lane, cols, g, b, eps, out + row * cols);
 }
 
+// LayerNorm of a 16-bit row stream with no residual operand (the model's path: the residual add
+// is fused into the GEMM before it).  Persistent warps walk rows with a stride and keep the next
+// row's raw 16-bit data in flight while they normalise the current one: twice the bytes in
+// flight per warp at the same occupancy (about 32 warps per SM at this register count), for
+// the DRAM latency that bounds a one-row-per-warp kernel.  Same arithmetic as k_add_ln.
+constexpr int kLnPipeWarps = 8;
+template <typename T, int PER, int VEC, int MINB>
+__global__ void __launch_bounds__(kLnPipeWarps * 32, MINB) k_ln_pipe(const T* __restrict__ x, T* __restrict__ out,
+                                                               const float* __restrict__ g,
+                                                               const float* __restrict__ b, int64_t rows, int cols,
+                                                               float eps) {
+  constexpr int NV = PER / VEC;
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * kLnPipeWarps;
+  int64_t row = (int64_t)blockIdx.x * kLnPipeWarps + (threadIdx.x >> 5);
+  Vec<T, VEC> cur[NV], nxt[NV];
+  if (row < rows) {
+#pragma unroll
+    for (int j = 0; j < NV; j++) cur[j] = *reinterpret_cast<const Vec<T, VEC>*>(x + row * cols + (j * 32 + lane) * VEC);
+  }
+  for (; row < rows; row += nw) {
+    const int64_t nr = row + nw;
+    if (nr < rows) {
+#pragma unroll
+      for (int j = 0; j < NV; j++) nxt[j] = *reinterpret_cast<const Vec<T, VEC>*>(x + nr * cols + (j * 32 + lane) * VEC);
+    }
+    float v[PER];
+#pragma unroll
+    for (int j = 0; j < NV; j++)
+#pragma unroll
+      for (int i = 0; i < VEC; i++) v[j * VEC + i] = to_f<T>(cur[j].d[i]);
+    ln_finish<T, PER, VEC>(v, lane, cols, g, b, eps, out + row * cols);
+#pragma unroll
+    for (int j = 0; j < NV; j++) cur[j] = nxt[j];
+  }
+}
+
 // Fallback for rows that are not a multiple of 32 elements or longer than 1024: one block per
 // row, three passes over global memory.
 template <typename T>
@@ -120,6 +158,23 @@ static int32_t add_ln_t(Ctx* c, const T* x, const T* res, T* out, const float* g
   const int grid = (int)((rows * 32 + 127) / 128);
   constexpr int V16 = sizeof(T) == 2 ? 8 : 4;
   bool done = true;
+  if constexpr (sizeof(T) == 2) {
+    if (!res && (cols == 768 || cols == 1024 || cols == 512 || cols == 256)) {
+      // Three 8-warp blocks per SM (80 registers, no spills); a fourth (forced to 64 registers)
+      // spilled and measured 38.1-38.4 against 35.9 us for a cfg3-sized LayerNorm.
+      const int64_t want = (rows + kLnPipeWarps - 1) / kLnPipeWarps;
+      const int grid2 = (int)std::min<int64_t>(want, (int64_t)c->num_sms * 3);
+#define FL_LNP2(PER_) \
+  FL_CUDA(c, launch_pdl(k_ln_pipe<T, PER_, 8, 3>, dim3(grid2), dim3(kLnPipeWarps * 32), 0, c->stream, x, out, g, b, rows, (int)cols, eps))
+      if (cols == 768) FL_LNP2(24);
+      else if (cols == 1024) FL_LNP2(32);
+      else if (cols == 512) FL_LNP2(16);
+      else FL_LNP2(8);
+#undef FL_LNP2
+      FL_LAUNCH(c);
+      return FLETCHER_OK;
+    }
+  }
   if (cols % 32 != 0) done = false;
 #define FL_LN(PER_, VEC_) \
   FL_CUDA(c, launch_pdl(k_add_ln<T, PER_, VEC_>, dim3(grid), dim3(128), 0, c->stream, x, res, out, g, b, rows, (int)cols, eps))
@@ -367,14 +422,25 @@ __global__ void __launch_bounds__(kLnPoolWarps * 32)
   float acc[PER];
 #pragma unroll
   for (int i = 0; i < PER; i++) acc[i] = 0.f;
+  constexpr int NV = PER / VEC;
+  Vec<T, VEC> cur[NV], nxt[NV];
+  if (a + warp < e) {
+#pragma unroll
+    for (int j = 0; j < NV; j++)
+      cur[j] = *reinterpret_cast<const Vec<T, VEC>*>(x + (int64_t)(a + warp) * cols + (j * 32 + lane) * VEC);
+  }
   for (int r = a + warp; r < e; r += kLnPoolWarps) {
+    if (r + kLnPoolWarps < e) {  // the warp's next row loads while this one is normalised
+#pragma unroll
+      for (int j = 0; j < NV; j++)
+        nxt[j] = *reinterpret_cast<const Vec<T, VEC>*>(x + (int64_t)(r + kLnPoolWarps) * cols + (j * 32 + lane) * VEC);
+    }
     float v[PER];
-    const T* xr = x + (int64_t)r * cols;
 #pragma unroll
-    for (int j = 0; j < PER / VEC; j++) {
-      Vec<T, VEC> t = *reinterpret_cast<const Vec<T, VEC>*>(xr + (j * 32 + lane) * VEC);
+    for (int j = 0; j < NV; j++) {
 #pragma unroll
-      for (int i = 0; i < VEC; i++) v[j * VEC + i] = to_f<T>(t.d[i]);
+      for (int i = 0; i < VEC; i++) v[j * VEC + i] = to_f<T>(cur[j].d[i]);
+      cur[j] = nxt[j];
     }
     float s = 0.f;
 #pragma unroll
