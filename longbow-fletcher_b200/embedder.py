@@ -227,6 +227,9 @@ class Server:
         busy = 0
         nrep = len(self.emb.replicas)
         jobs = [0] * nrep
+        # One batch takes at most its replica's share of the in-flight budget, so that every
+        # replica can hold work at once under the cap.
+        share = max(1, self.max_in_flight // (nrep * self.jobs_per_replica))
         while not self.stop or not self.q.empty() or held:
             if not held:
                 try:
@@ -246,8 +249,13 @@ class Server:
                     rep = i
                     break
             reqs, nseq = [], 0
-            while rep is not None and held and (busy + nseq + len(held[0][2]) <= self.max_in_flight
-                                                or (busy == 0 and not reqs)):
+
+            def fits(n):
+                if not reqs:  # a batch's first request: within the budget, or alone when nothing runs
+                    return busy + n <= self.max_in_flight or busy == 0
+                return busy + nseq + n <= self.max_in_flight and nseq + n <= share
+
+            while rep is not None and held and fits(len(held[0][2])):
                 r = held.popleft()
                 reqs.append(r)
                 nseq += len(r[2])

@@ -89,3 +89,17 @@ def test_arrival_time_counts_in_latency():
     _, lat = srv.submit(ids, lens, arrival=t0).result(timeout=10)
     assert lat >= 0.5
     srv.close()
+
+
+def test_budget_is_shared_by_the_replicas():
+    """Under a saturating load every replica holds work at once: no single batch takes more than
+    its share of the in-flight budget."""
+    emb = FakeEmbedder(4, 0.02)
+    srv = embedder.Server(emb, max_in_flight=64, jobs_per_replica=2)
+    reqs = _requests(300, seed=2)
+    futs = [srv.submit(*r) for r in reqs]
+    for f in futs:
+        f.result(timeout=60)
+    srv.close()
+    assert max(n for _, n in emb.log) <= max(64 // 8, 16)  # one request may exceed the share alone
+    assert {id(r) for r, _ in emb.log} == {id(r) for r in emb.replicas}
