@@ -297,14 +297,17 @@ def main():
             run_ops_route(args, w)
         return
 
+    if world > 1:
+        # NCCL's communicator set-up lines (ranks, transport) go to stderr for the record; the
+        # communicator carries only the barrier and the max-over-ranks of the timings.  Set before
+        # torch loads NCCL.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT,ENV")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")  # stdout carries only the JSON line
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(local)
     if world > 1:
-        # NCCL's communicator set-up lines (ranks, transport) go to stderr for the record; the
-        # communicator carries only the barrier and the max-over-ranks of the timings.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     import fletcher as fl
 
