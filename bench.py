@@ -43,9 +43,9 @@ METRIC = "embeddings/sec (nomic-embed-text seq512 bf16)"
 # of one nomic layer, per token, from one capture of a cfg3 forward; scaled to the timed
 # forwards.  Not measured per run (a bench run is never profiled); GEMM_TRAFFIC_NOTE names the
 # capture it comes from.
-GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 25625.0
-GEMM_TRAFFIC_NOTE = ("ncu dram bytes per token per layer of the 4 GEMMs (1680 MB for 65.6K tokens, one cfg3 "
-                     "capture of the GEMM kernel as of commit 780f7e2), scaled to the timed forwards")
+GEMM_DRAM_BYTES_PER_TOKEN_LAYER = 25822.0
+GEMM_TRAFFIC_NOTE = ("ncu dram bytes per token per layer of the 4 GEMMs (1692.8 MB for 65,557 tokens, one cfg3 "
+                     "capture of the GEMM kernel as of commit ba46dbf), scaled to the timed forwards")
 
 
 def peaks():

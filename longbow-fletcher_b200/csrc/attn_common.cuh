@@ -26,19 +26,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
-// Packed two-lane fp32 FMA / add (sm_100): one instruction for two values.
-__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
-  asm("{\n .reg .b64 a, b, c, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n mov.b64 c, {%6, %7};\n"
-      " fma.rn.f32x2 d, a, b, c;\n mov.b64 {%0, %1}, d;\n}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
-}
-__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1) {
-  asm("{\n .reg .b64 a, d;\n mov.b64 d, {%0, %1};\n mov.b64 a, {%2, %3};\n add.rn.f32x2 d, d, a;\n"
-      " mov.b64 {%0, %1}, d;\n}"
-      : "+f"(d0), "+f"(d1)
-      : "f"(a0), "f"(a1));
-}
 // Keys at and past `valid` lie outside the sequence.
 template <int N>
 __device__ __forceinline__ void mask_tail(float (&sv)[N], int valid) {

@@ -83,6 +83,40 @@ __global__ void __launch_bounds__(128) k_add_ln(const T* __restrict__ x, const T
 // row's raw 16-bit data in flight while they normalise the current one: twice the bytes in
 // flight per warp at the same occupancy (about 32 warps per SM at this register count), for
 // the DRAM latency that bounds a one-row-per-warp kernel.  Same arithmetic as k_add_ln.
+// LayerNorm of a row held as PER values per lane (lanes own 16-byte groups (j*32 + lane)*VEC),
+// in packed f32x2 arithmetic: two-pass statistics (mean, then the mean of squared deviations),
+// inv = 1/float32(sqrt(float64(var + eps))), y = (x - mean) * inv * gamma + beta with the last
+// step fused.  Half the instructions of the scalar form; results differ from it by fp32
+// rounding only.  v holds y on return.
+template <int PER, int VEC>
+__device__ __forceinline__ void ln_row_x2(float (&v)[PER], int lane, int cols, const float* __restrict__ g,
+                                          const float* __restrict__ b, float eps) {
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; i += 2) add2(s0, s1, v[i], v[i + 1]);
+  const float mean = __fdiv_rn(warp_sum(s0 + s1), (float)cols);
+  float q0 = 0.f, q1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; i += 2) {
+    add2(v[i], v[i + 1], -mean, -mean);
+    fma2(q0, q1, v[i], v[i + 1], v[i], v[i + 1], q0, q1);
+  }
+  const float var = __fdiv_rn(warp_sum(q0 + q1), (float)cols);
+  const float inv = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(var, eps)));
+#pragma unroll
+  for (int j = 0; j < PER / VEC; j++) {
+    const int e = (j * 32 + lane) * VEC;
+    Vec<float, VEC> gv = *reinterpret_cast<const Vec<float, VEC>*>(g + e);
+    Vec<float, VEC> bv = *reinterpret_cast<const Vec<float, VEC>*>(b + e);
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      float* y = &v[j * VEC + i];
+      mul2(y[0], y[1], y[0], y[1], inv, inv);
+      fma2(y[0], y[1], y[0], y[1], gv.d[i], gv.d[i + 1], bv.d[i], bv.d[i + 1]);
+    }
+  }
+}
+
 constexpr int kLnPipeWarps = 8;
 template <typename T, int PER, int VEC, int MINB>
 __global__ void __launch_bounds__(kLnPipeWarps * 32, MINB) k_ln_pipe(const T* __restrict__ x, T* __restrict__ out,
@@ -110,9 +144,16 @@ __global__ void __launch_bounds__(kLnPipeWarps * 32, MINB) k_ln_pipe(const T* __
     for (int j = 0; j < NV; j++)
 #pragma unroll
       for (int i = 0; i < VEC; i++) v[j * VEC + i] = to_f<T>(cur[j].d[i]);
-    ln_finish<T, PER, VEC>(v, lane, cols, g, b, eps, out + row * cols);
+    ln_row_x2<PER, VEC>(v, lane, cols, g, b, eps);
+    T* orow = out + row * cols;
 #pragma unroll
-    for (int j = 0; j < NV; j++) cur[j] = nxt[j];
+    for (int j = 0; j < NV; j++) {
+      Vec<T, VEC> o;
+#pragma unroll
+      for (int i = 0; i < VEC; i++) o.d[i] = from_f<T>(v[j * VEC + i]);
+      *reinterpret_cast<Vec<T, VEC>*>(orow + (j * 32 + lane) * VEC) = o;
+      cur[j] = nxt[j];
+    }
   }
 }
 
@@ -403,8 +444,8 @@ int32_t launch_mean_pool_l2(Ctx* c, int32_t dt, const void* h, const int32_t* cu
 // The last layer's LayerNorm and the mean-pool + L2 head in two passes, without writing the
 // normalised [T, H] rows: stage 1 takes a chunk of up to kLnPoolRows rows of one sequence (grid:
 // chunks x sequences; chunks past a sequence's end exit), normalises each row in registers with
-// the LayerNorm kernel's arithmetic (one warp per row, rounded to the model dtype exactly as the
-// LayerNorm kernel stores it) and writes the chunk's fp32 column sums; stage 2 adds a sequence's
+// k_ln_pipe's arithmetic (one warp per row, rounded to the model dtype exactly as k_ln_pipe
+// stores it) and writes the chunk's fp32 column sums; stage 2 adds a sequence's
 // chunk sums in chunk order, divides by its length and L2-normalises.  Deterministic: the same
 // summation order on every run.
 constexpr int kLnPoolRows = 64, kLnPoolWarps = 8;
@@ -442,30 +483,9 @@ __global__ void __launch_bounds__(kLnPoolWarps * 32)
       for (int i = 0; i < VEC; i++) v[j * VEC + i] = to_f<T>(cur[j].d[i]);
       cur[j] = nxt[j];
     }
-    float s = 0.f;
+    ln_row_x2<PER, VEC>(v, lane, cols, g, b, eps);  // the same arithmetic as k_ln_pipe
 #pragma unroll
-    for (int i = 0; i < PER; i++) s += v[i];
-    s = warp_sum(s);
-    const float mean = __fdiv_rn(s, (float)cols);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < PER; i++) {
-      float d = __fsub_rn(v[i], mean);
-      q = __fadd_rn(q, __fmul_rn(d, d));
-    }
-    q = warp_sum(q);
-    const float var = __fdiv_rn(q, (float)cols);
-    const float inv = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(var, eps)));
-#pragma unroll
-    for (int j = 0; j < PER / VEC; j++) {
-      const int e0 = (j * 32 + lane) * VEC;
-      Vec<float, VEC> gv = *reinterpret_cast<const Vec<float, VEC>*>(g + e0);
-      Vec<float, VEC> bv = *reinterpret_cast<const Vec<float, VEC>*>(b + e0);
-#pragma unroll
-      for (int i = 0; i < VEC; i++)
-        acc[j * VEC + i] += to_f<T>(
-            from_f<T>(__fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j * VEC + i], mean), inv), gv.d[i]), bv.d[i])));
-    }
+    for (int i = 0; i < PER; i++) acc[i] += to_f<T>(from_f<T>(v[i]));  // rounded as the stored rows would be
   }
 #pragma unroll
   for (int j = 0; j < PER / VEC; j++)
