@@ -23,7 +23,6 @@
 // TMEM per slot: S/P 64 columns + O 64 columns; 256 per CTA.  ~98 KB smem.  All mbarrier waits
 // are bounded (device error flag + abort, as in the GEMM).  No multicast.
 #include <atomic>
-#include <cstdlib>
 
 #include "attn_common.cuh"
 
@@ -402,16 +401,13 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void*
                   ((uintptr_t)v & 15) == 0 && ((uintptr_t)out & 15) == 0,
            "attention_tc: rows must be 16-byte aligned");
   FL_CHECK(c, (int64_t)num_tiles * nh < (1ll << 31), "attention_tc: too many work items");
-  static const int db = [] {
-    const char* e = getenv("FLETCHER_ATTN_DB");
-    return e ? atoi(e) : 0;
-  }();
-  if (db) return launch_flash_attention_db(c, dt, q, k, v, ld_in, T, H, out, ld_out, tiles128, num_tiles, nh, scale);
   // 64-key blocks, two slots per CTA, two CTAs per SM.  Two other shapes measured slower, A/B on
   // one box at 1.91-1.97 GHz (attention ms per cfg3 step): 128-key blocks with one slot per CTA
   // (N = 128 MMAs for S, half the slots per SM) 2.70-2.75 against 2.24-2.30; two query tiles of a
   // sequence sharing each K/V block with P in shared memory and S_{j+1} issued before PV_j, one
-  // control thread for both tiles, 3.10 against 2.30-2.32.
+  // control thread for both tiles, 3.10 against 2.30-2.32; one slot per CTA with S double-buffered
+  // in TMEM (S_{j+2} issued right after PV_j, so the softmax never waits for S) 3.25-3.28 against
+  // 2.28-2.29: with half the slots per SM the softmax warps, not the S round trip, set the pace.
   if (dt == FLETCHER_BF16)
     return launch_attn_variant<__nv_bfloat16, 64, 2>(c, dt, q, k, v, ld_in, T, H, out, ld_out, cu, tiles128, num_tiles,
                                                      nh, scale);

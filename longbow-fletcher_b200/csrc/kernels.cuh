@@ -67,10 +67,6 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dtype, const void* q, const vo
                                   int64_t ld_in, int64_t T, int64_t H, void* out, int64_t ld_out,
                                   const int32_t* cu_seqlens, const int2* tiles128, int32_t num_tiles,
                                   int32_t nh, float scale);
-// The same attention with S double-buffered in tensor memory, one slot per CTA (attention_db.cu).
-int32_t launch_flash_attention_db(Ctx* c, int32_t dtype, const void* q, const void* k, const void* v, int64_t ld_in,
-                                  int64_t T, int64_t H, void* out, int64_t ld_out, const int2* tiles128,
-                                  int32_t num_tiles, int32_t nh, float scale);
 // Query-tile height of launch_flash_attention_tc, and the longest sequence it takes.
 constexpr int kAttnTileRows = 128;
 constexpr int kAttnMaxLen = 65535;
