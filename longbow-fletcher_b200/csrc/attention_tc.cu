@@ -407,7 +407,9 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void*
   // sequence sharing each K/V block with P in shared memory and S_{j+1} issued before PV_j, one
   // control thread for both tiles, 3.10 against 2.30-2.32; one slot per CTA with S double-buffered
   // in TMEM (S_{j+2} issued right after PV_j, so the softmax never waits for S) 3.25-3.28 against
-  // 2.28-2.29: with half the slots per SM the softmax warps, not the S round trip, set the pace.
+  // 2.28-2.29: with half the slots per SM the softmax warps, not the S round trip, set the pace;
+  // eight softmax warps per slot, two per TMEM lane quarter each taking half of a row's keys (their
+  // halves meeting through a pair mbarrier), 2.75-2.78 against 2.27.
   if (dt == FLETCHER_BF16)
     return launch_attn_variant<__nv_bfloat16, 64, 2>(c, dt, q, k, v, ld_in, T, H, out, ld_out, cu, tiles128, num_tiles,
                                                      nh, scale);
