@@ -418,7 +418,9 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void*
   // in TMEM (S_{j+2} issued right after PV_j, so the softmax never waits for S) 3.25-3.28 against
   // 2.28-2.29: with half the slots per SM the softmax warps, not the S round trip, set the pace;
   // eight softmax warps per slot, two per TMEM lane quarter each taking half of a row's keys (their
-  // halves meeting through a pair mbarrier), 2.75-2.78 against 2.27.
+  // halves meeting through a pair mbarrier), 2.75-2.78 against 2.27; the exponentials as
+  // ex2.approx.f16x2 (half the MUFU instructions, fp16 exponents, P range 2^15) 2.56-2.63 against
+  // 2.27-2.30: the extra conversions cost more than the MUFU time saved.
   static const bool e16 = [] {
     const char* e = getenv("FLETCHER_ATTN_EXP16");
     return e && atoi(e) == 1;
