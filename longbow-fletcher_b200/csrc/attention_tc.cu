@@ -23,7 +23,6 @@
 // TMEM per slot: S/P 64 columns + O 64 columns; 256 per CTA.  ~98 KB smem.  All mbarrier waits
 // are bounded (device error flag + abort, as in the GEMM).  No multicast.
 #include <atomic>
-#include <cstdlib>
 
 #include "attn_common.cuh"
 
@@ -92,7 +91,7 @@ __device__ __forceinline__ Work decode(const AttnArgs& a, int w) {
   return r;
 }
 
-template <typename T, int BKV_, int SLOTS_, bool EXP16 = false>
+template <typename T, int BKV_, int SLOTS_>
 __global__ void __launch_bounds__(AttnCfg<BKV_, SLOTS_>::kThreads, 2)
     k_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
               const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
@@ -277,14 +276,11 @@ __global__ void __launch_bounds__(AttnCfg<BKV_, SLOTS_>::kThreads, 2)
         if (j == 0) m_ref = sv[0];
         float rsum;
         uint32_t pk[BKV / 2];
-        if constexpr (EXP16)
-          exp_row_h2<T, BKV>(sv, sl2, m_ref * sl2, pk, rsum);
-        else
-          exp_row<T, BKV>(sv, sl2, m_ref * sl2, pk, rsum);
+        exp_row<T, BKV>(sv, sl2, m_ref * sl2, pk, rsum);
         // The row sum bounds every P of the row, so a sum within the P range proves that no P
         // left it (a NaN fails the test too).  A sum beyond the range with every P inside it only
         // costs a needless rescale.
-        const bool need = !(rsum <= (EXP16 ? 32768.0f : kPMax<T>()));
+        const bool need = !(rsum <= kPMax<T>());
         if (__any_sync(0xffffffffu, need)) {
           // Rare path: some row's max moved by more than the P range allows.  S is still in
           // TMEM (P is not written yet); O holds PV_0..PV_{j-1} complete (S_j's commit came
@@ -311,10 +307,7 @@ __global__ void __launch_bounds__(AttnCfg<BKV_, SLOTS_>::kThreads, 2)
           }
           tmem_ld_row<BKV>(t_s, sv);
           if (valid < BKV) mask_tail(sv, valid);
-          if constexpr (EXP16)
-            exp_row_h2<T, BKV>(sv, sl2, m_ref * sl2, pk, rsum);
-          else
-            exp_row<T, BKV>(sv, sl2, m_ref * sl2, pk, rsum);
+          exp_row<T, BKV>(sv, sl2, m_ref * sl2, pk, rsum);
         }
         tmem_st_p<BKV>(t_p, pk);
         tmem_st_wait();
@@ -371,7 +364,7 @@ __global__ void __launch_bounds__(AttnCfg<BKV_, SLOTS_>::kThreads, 2)
 int32_t make_tma_map_2d(Ctx* c, CUtensorMap* m, int32_t dtype, const void* ptr, uint64_t rows, uint64_t cols,
                         uint64_t ld, uint32_t box_cols, uint32_t box_rows);
 
-template <typename T, int BKV, int SLOTS, bool EXP16 = false>
+template <typename T, int BKV, int SLOTS>
 static int32_t launch_attn_variant(Ctx* c, int32_t dt, const void* q, const void* k, const void* v, int64_t ld_in,
                                    int64_t T_, int64_t H, void* out, int64_t ld_out, const int32_t* cu,
                                    const int2* tiles128, int32_t num_tiles, int32_t nh, float scale) {
@@ -388,14 +381,12 @@ static int32_t launch_attn_variant(Ctx* c, int32_t dt, const void* q, const void
   // Per device; host threads of several replicas may get here at once (idempotent).
   static std::atomic<bool> attr_set[64] = {};
   if (!attr_set[c->device & 63].load(std::memory_order_acquire)) {
-    FL_CUDA(c, cudaFuncSetAttribute(k_attn_tc<T, BKV, SLOTS, EXP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::SMEM));
+    FL_CUDA(c, cudaFuncSetAttribute(k_attn_tc<T, BKV, SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set[c->device & 63].store(true, std::memory_order_release);
   }
   const int want = (work + SLOTS - 1) / SLOTS;
   const int grid = want < 2 * c->num_sms ? want : 2 * c->num_sms;
-  FL_CUDA(c, launch_pdl(k_attn_tc<T, BKV, SLOTS, EXP16>, dim3(grid), dim3(C::kThreads), C::SMEM, c->stream, mq, mk,
-                        mv, a));
+  FL_CUDA(c, launch_pdl(k_attn_tc<T, BKV, SLOTS>, dim3(grid), dim3(C::kThreads), C::SMEM, c->stream, mq, mk, mv, a));
   FL_LAUNCH(c);
   return FLETCHER_OK;
 }
@@ -421,17 +412,6 @@ int32_t launch_flash_attention_tc(Ctx* c, int32_t dt, const void* q, const void*
   // halves meeting through a pair mbarrier), 2.75-2.78 against 2.27; the exponentials as
   // ex2.approx.f16x2 (half the MUFU instructions, fp16 exponents, P range 2^15) 2.56-2.63 against
   // 2.27-2.30: the extra conversions cost more than the MUFU time saved.
-  static const bool e16 = [] {
-    const char* e = getenv("FLETCHER_ATTN_EXP16");
-    return e && atoi(e) == 1;
-  }();
-  if (e16) {
-    if (dt == FLETCHER_BF16)
-      return launch_attn_variant<__nv_bfloat16, 64, 2, true>(c, dt, q, k, v, ld_in, T, H, out, ld_out, cu, tiles128,
-                                                             num_tiles, nh, scale);
-    return launch_attn_variant<__half, 64, 2, true>(c, dt, q, k, v, ld_in, T, H, out, ld_out, cu, tiles128, num_tiles,
-                                                    nh, scale);
-  }
   if (dt == FLETCHER_BF16)
     return launch_attn_variant<__nv_bfloat16, 64, 2>(c, dt, q, k, v, ld_in, T, H, out, ld_out, cu, tiles128, num_tiles,
                                                      nh, scale);

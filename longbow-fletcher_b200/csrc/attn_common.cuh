@@ -68,32 +68,6 @@ __device__ __forceinline__ void exp_row(float (&sv)[N], float sl2, float ms, uin
   sum = ((ra[0][0] + ra[0][1]) + (ra[1][0] + ra[1][1])) + ((ra[2][0] + ra[2][1]) + (ra[3][0] + ra[3][1]));
 }
 
-// exp_row with the exponentials on the half-precision MUFU path: the exponents are rounded to
-// fp16 pairs and ex2.approx.f16x2 produces two P values per instruction (half the MUFU work);
-// the sum is taken from the widened fp16 results.  P stays below 2^15 (the fp16 range) by the
-// caller's range check.
-template <typename T, int N>
-__device__ __forceinline__ void exp_row_h2(float (&sv)[N], float sl2, float ms, uint32_t (&pk)[N / 2], float& sum) {
-  float ra[4][2] = {};
-#pragma unroll
-  for (int i = 0; i < N; i += 2) {
-    fma2(sv[i], sv[i + 1], sv[i], sv[i + 1], sl2, sl2, -ms, -ms);
-    uint32_t h2;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(sv[i + 1]), "f"(sv[i]));  // low half = element i
-    asm("ex2.approx.f16x2 %0, %0;" : "+r"(h2));
-    float lo, hi;
-    asm("{\n .reg .f16 l, h;\n mov.b32 {l, h}, %2;\n cvt.f32.f16 %0, l;\n cvt.f32.f16 %1, h;\n}"
-        : "=f"(lo), "=f"(hi)
-        : "r"(h2));
-    add2(ra[(i >> 1) & 3][0], ra[(i >> 1) & 3][1], lo, hi);
-    if constexpr (std::is_same<T, __half>::value)
-      pk[i >> 1] = h2;
-    else
-      pk[i >> 1] = pack2<T>(lo, hi);
-  }
-  sum = ((ra[0][0] + ra[0][1]) + (ra[1][0] + ra[1][1])) + ((ra[2][0] + ra[2][1]) + (ra[3][0] + ra[3][1]));
-}
-
 // A row of N fp32 S columns (N = 64 or 128) with one wait.
 template <int N>
 __device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[N]) {
