@@ -331,6 +331,90 @@ int32_t Cuda_Model_LastHidden(CudaModelRef model, float* host_out, int64_t count
 int32_t Cuda_Model_SetKeepHidden(CudaModelRef model, int32_t enable);
 int32_t Cuda_Model_Free(CudaModelRef model);
 
+/* ---- Host runtime: multi-GPU embedder and request server (internal/embeddings/embeddings.go)
+ *
+ * Native restatement of the reference's Embedder: one model replica per device, each driven by
+ * its own host thread that keeps two device batches in flight (Cuda_Model_ForwardBatchAsync into
+ * pinned buffers), requests split across replicas by token count weighted by each replica's
+ * measured throughput (embeddings.go:436-501) and cut into dynamic batches of at most max_batch
+ * sequences / max_tokens tokens (embeddings.go:704-731); and of its server front end: a request
+ * queue whose batcher keeps at most max_in_flight sequences handed to the replicas (server.go:101,
+ * the sequence semaphore) and dispatches batches round-robin to replicas holding fewer than
+ * jobs_per_replica batches.  Packing ([CLS] ids [SEP] per text, embeddings.go:742-749) and
+ * tokenisation stay with the caller. */
+typedef void* CudaEmbedderRef;
+typedef void* CudaServerRef;
+
+/* Replicas over existing models, one per element of models[] (each on its own context; two
+ * models may share a device).  The embedder drives the models from its own threads: do not call
+ * them elsewhere while it runs.  pooling: FLETCHER_POOL_*.  max_tokens <= 0: 65536 tokens per
+ * batch on devices with >= 64 GB, else 16384 (the reference's VRAM-dependent default,
+ * embeddings.go:177-190). */
+int32_t Cuda_Embedder_Create(const CudaModelRef* models, int32_t n, int32_t pooling, int32_t max_batch,
+                             int64_t max_tokens, CudaEmbedderRef* out);
+/* Test double with no GPU: n replicas that return, for sequence i of a batch, the vector
+ * (first id, length, replica index, 0, ...) of width `hidden`, after sleeping delay_us per batch. */
+int32_t Cuda_Embedder_CreateFake(int32_t n, int32_t hidden, int64_t delay_us, int32_t max_batch,
+                                 int64_t max_tokens, CudaEmbedderRef* out);
+/* Embeds packed ids / lengths (numSeqs sequences) into out[numSeqs, hidden] (float32, request
+ * order).  Synchronous; may run concurrently with a server on the same embedder. */
+int32_t Cuda_Embedder_Embed(CudaEmbedderRef e, const int32_t* ids, const int32_t* lengths, int32_t numSeqs,
+                            float* out);
+/* Per-replica throughput in sequences/s: 1.0 until the first batch finishes, then that batch's
+ * rate, then an exponential average with weight 0.3 on each new batch (embeddings.go:197,
+ * 795-804).  Read into tput[n], or set from tput[n] when set != 0. */
+int32_t Cuda_Embedder_Throughput(CudaEmbedderRef e, double* tput, int32_t n, int32_t set);
+/* Per-replica counters since creation: batches handed to the replica (jobs) and their sequences. */
+int32_t Cuda_Embedder_Counts(CudaEmbedderRef e, int64_t* jobs, int64_t* seqs, int32_t n);
+int32_t Cuda_Embedder_Hidden(CudaEmbedderRef e);
+int32_t Cuda_Embedder_MaxBatch(CudaEmbedderRef e, int32_t* max_batch, int64_t* max_tokens);
+/* Text of the last failed call on this embedder (or of a failed request of its servers). */
+int32_t Cuda_Embedder_LastError(CudaEmbedderRef e, char* buf, int32_t len);
+/* Stops the replica threads (after their queued work).  Does not free the models.  Destroy the
+ * embedder's servers first. */
+void Cuda_Embedder_Destroy(CudaEmbedderRef e);
+
+/* Request server over an embedder.  max_in_flight <= 0: 16384; jobs_per_replica <= 0: 2. */
+int32_t Cuda_Server_Create(CudaEmbedderRef e, int32_t max_in_flight, int32_t jobs_per_replica, CudaServerRef* out);
+/* Enqueues n requests.  Request r holds the sequences seq_off[r] .. seq_off[r+1]-1 of
+ * lengths[] (seq_off has n+1 entries, seq_off[0] = 0), whose ids lie packed in ids[] in that
+ * order; its vectors go to out + seq_off[r] * hidden.  ids and lengths are copied before the call
+ * returns; out must stay valid until the request completes.  arrival_ns (may be NULL): each
+ * request's arrival on Cuda_Server_Clock's clock, from which its latency counts (an open-loop
+ * load schedule); otherwise latency counts from this call.  The requests get consecutive
+ * tickets starting at *first_ticket (>= 1). */
+int32_t Cuda_Server_Submit(CudaServerRef s, int32_t n, const int32_t* ids, const int32_t* lengths,
+                           const int64_t* seq_off, const int64_t* arrival_ns, float* out, int64_t* first_ticket);
+/* Monotonic clock of the server, nanoseconds. */
+int64_t Cuda_Server_Clock(void);
+/* Waits up to timeout_s seconds (< 0: no limit) for request `ticket`.  Returns its status
+ * (FLETCHER_OK, an error of its batch, or FLETCHER_ERR_INVALID for an unknown ticket); a wait
+ * that times out returns -1.  *latency_ns (may be NULL) receives the request's latency. */
+int32_t Cuda_Server_Wait(CudaServerRef s, int64_t ticket, double timeout_s, int64_t* latency_ns);
+/* Latencies of tickets first .. first+n-1 (-1: not complete, -2: failed). */
+int32_t Cuda_Server_Latencies(CudaServerRef s, int64_t first, int64_t n, int64_t* latency_ns);
+/* Waits until every submitted request has completed. */
+int32_t Cuda_Server_Drain(CudaServerRef s);
+typedef struct FletcherServerStats {
+  int64_t requests;        /* submitted */
+  int64_t completed;
+  int64_t batches;         /* batches handed to replicas */
+  int64_t max_batch_seqs;  /* largest batch made of two or more requests */
+  int64_t max_request_seqs;/* largest single request */
+  int64_t max_busy;        /* most sequences in flight at once */
+} FletcherServerStats;
+int32_t Cuda_Server_Stats(CudaServerRef s, FletcherServerStats* st);
+/* Completes every submitted request, then stops the batcher. */
+void Cuda_Server_Destroy(CudaServerRef s);
+/* The reference's split and batching rules, exported for callers and tests.  SplitByWeight:
+ * contiguous [ranges[2d], ranges[2d+1]) of the numSeqs sequences per replica d (n replicas,
+ * weights = throughputs, all 0 = equal shares); returns the number of replicas that got a range.
+ * DynamicBatches: [start, end) pairs into ranges (capacity cap pairs); returns the count. */
+int32_t Cuda_Runtime_SplitByWeight(const int32_t* lengths, int32_t numSeqs, const double* weights, int32_t n,
+                                   int32_t* ranges);
+int32_t Cuda_Runtime_DynamicBatches(const int32_t* lengths, int32_t numSeqs, int32_t max_batch, int64_t max_tokens,
+                                    int32_t* ranges, int32_t cap);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -21,7 +21,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-DFLETCHER_BUILD"]
 SOURCES = ["context.cu", "ops.cu", "gemm_simt.cu", "gemm_tc.cu", "attention.cu", "model.cu", "abi_ops.cu",
-           "noalloc.cu", "attention_tc.cu", "probe.cu"]
+           "noalloc.cu", "attention_tc.cu", "probe.cu", "runtime.cu"]
 
 
 def _deps():

@@ -1075,6 +1075,14 @@ int32_t Cuda_Model_StageTimes(CudaModelRef model, float* ms, int64_t* launches, 
   return FLETCHER_OK;
 }
 
+}  // extern "C"
+
+// The host runtime (runtime.cu) reads a model's width and context through these.
+int64_t model_hidden(CudaModelRef model) { return model ? reinterpret_cast<Model*>(model)->H : 0; }
+CudaContextRef model_context(CudaModelRef model) { return model ? reinterpret_cast<Model*>(model)->c : nullptr; }
+
+extern "C" {
+
 int32_t Cuda_Model_Free(CudaModelRef model) {
   Model* m = reinterpret_cast<Model*>(model);
   if (!m) return FLETCHER_OK;

@@ -106,6 +106,25 @@ def _sig(L):
         "Cuda_Copy": (i32, [vp, vp, i64, vp, i64, i64]),
         "Cuda_Slice": (i32, [vp, vp, i64, i64, i64, i64, vp]),
         "Cuda_Mul": (i32, [vp, vp, i32, vp, i32, vp, i64, i64, i64]),
+        "Cuda_Embedder_Create": (i32, [ctypes.POINTER(vp), i32, i32, i32, i64, ctypes.POINTER(vp)]),
+        "Cuda_Embedder_CreateFake": (i32, [i32, i32, i64, i32, i64, ctypes.POINTER(vp)]),
+        "Cuda_Embedder_Embed": (i32, [vp, i32p, i32p, i32, f32p]),
+        "Cuda_Embedder_Throughput": (i32, [vp, ctypes.POINTER(ctypes.c_double), i32, i32]),
+        "Cuda_Embedder_Counts": (i32, [vp, i64p, i64p, i32]),
+        "Cuda_Embedder_Hidden": (i32, [vp]),
+        "Cuda_Embedder_MaxBatch": (i32, [vp, i32p, i64p]),
+        "Cuda_Embedder_LastError": (i32, [vp, ctypes.c_char_p, i32]),
+        "Cuda_Embedder_Destroy": (None, [vp]),
+        "Cuda_Server_Create": (i32, [vp, i32, i32, ctypes.POINTER(vp)]),
+        "Cuda_Server_Submit": (i32, [vp, i32, i32p, i32p, i64p, i64p, f32p, i64p]),
+        "Cuda_Server_Clock": (i64, []),
+        "Cuda_Server_Wait": (i32, [vp, i64, ctypes.c_double, i64p]),
+        "Cuda_Server_Latencies": (i32, [vp, i64, i64, i64p]),
+        "Cuda_Server_Drain": (i32, [vp]),
+        "Cuda_Server_Stats": (i32, [vp, vp]),
+        "Cuda_Server_Destroy": (None, [vp]),
+        "Cuda_Runtime_SplitByWeight": (i32, [i32p, i32, ctypes.POINTER(ctypes.c_double), i32, i32p]),
+        "Cuda_Runtime_DynamicBatches": (i32, [i32p, i32, i32, i64, i32p, i32]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
