@@ -16,7 +16,7 @@ Printed (rank 0, one JSON line):
             Cuda_Model_Wait, two batches in flight) with pinned host ids in and host vectors out
             (every step's H2D + D2H inside the timed region);
   roofline  the tensor-core GEMMs (the dominant kernels): algorithmic FLOPs / their event-timed
-            duration, against the measured sustained bf16 peak;
+            duration, against the measured burst bf16 peak (the sustained one beside it);
   cpu_baseline  the CPU oracle (C++ restatement of the reference's CPU path, OpenBLAS sgemm)
             on a bounded sample of the same workload, all host cores (rank 0, N=1 only).
 --impl reference times that CPU implementation alone as the reference arm.
