@@ -382,7 +382,9 @@ int32_t Cuda_Server_Create(CudaEmbedderRef e, int32_t max_in_flight, int32_t job
  * returns; out must stay valid until the request completes.  arrival_ns (may be NULL): each
  * request's arrival on Cuda_Server_Clock's clock, from which its latency counts (an open-loop
  * load schedule); otherwise latency counts from this call.  The requests get consecutive
- * tickets starting at *first_ticket (>= 1). */
+ * tickets starting at *first_ticket (>= 1).  A request's ids are freed once its batch completes;
+ * its completion record (arrival, completion time, status: about 100 bytes) stays until
+ * Cuda_Server_Destroy, so a long-running server holds about 100 MB per million requests. */
 int32_t Cuda_Server_Submit(CudaServerRef s, int32_t n, const int32_t* ids, const int32_t* lengths,
                            const int64_t* seq_off, const int64_t* arrival_ns, float* out, int64_t* first_ticket);
 /* Monotonic clock of the server, nanoseconds. */
